@@ -1,0 +1,462 @@
+#!/usr/bin/env python
+"""Benchmark of the cooperative-matrix GEMM / flash-attention path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl lvb|reference]
+
+One step = one call of the hot path over one batch of synthetic input, already resident in
+HBM. The default workload is BASELINE config 2, the fp16 GEMM M=N=K=8192 (fp32 accumulate,
+fp16 C) on one GPU; with N GPUs (torchrun, one rank per GPU) every rank runs its own
+8192-row shard of A against a replicated B (rows of A are independent: weak scaling, no
+collective on the data path). Rank 0 prints one JSON line: whole-job TFLOP/s over the max
+of the ranks' device times, plus roofline, end-to-end (host buffers, copies inside the
+timed region), CPU baseline and SM clocks sampled during the timed region.
+
+``--impl reference`` times the reference's CPU path stand-in (the oracle port: host
+float32 BLAS, or exact float64 BLAS for int8, or blockwise float32 attention) on the host
+cores — Lava's own path (Lava→SPIR-V on lavapipe, host Julia BLAS) needs Julia and a
+graphics stack, which this box does not have.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "lava.jl_b200"
+for _p in (str(REPO), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "GEMM / attention TFLOPS (and % dense tensor peak) at 1/2/4/8 B200"
+
+WORKLOADS = {
+    # name: (kind, config, shape per GPU)
+    "gemm_f16": dict(kind="gemm", cfg="C2", M=8192, N=8192, K=8192, ab="Float16", out="Float16",
+                     seed=1, dtype="f16"),
+    "gemm_f16_512": dict(kind="gemm", cfg="C1", M=512, N=512, K=512, ab="Float16", out="Float32",
+                         seed=0, dtype="f16"),
+    "gemm_i8": dict(kind="gemm", cfg="C3", M=8192, N=8192, K=8192, ab="Int8", out="Int32",
+                    seed=2, dtype="int8"),
+    "gemm_bf16": dict(kind="gemm", cfg="C5-gemm", M=65536, N=8192, K=8192, ab="BFloat16",
+                      out="BFloat16", seed=5, dtype="bf16"),
+    "attn_f16": dict(kind="attn", cfg="C4", B=4, Hq=32, Hkv=32, S=4096, D=128, ab="Float16",
+                     causal=True, seed=3, dtype="f16"),
+    "attn_bf16": dict(kind="attn", cfg="C5-attn", B=8, Hq=64, Hkv=8, S=16384, D=128,
+                      ab="BFloat16", causal=True, seed=4, dtype="bf16"),
+}
+
+
+def work_units(w) -> float:
+    if w["kind"] == "gemm":
+        return 2.0 * w["M"] * w["N"] * w["K"]
+    f = 4.0 * w["B"] * w["Hq"] * w["S"] * w["S"] * w["D"]
+    return f / 2 if w["causal"] else f
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic(workload: str):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    f = REPO / "profiles" / f"{workload}_ncu.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ----------------------------------------------------------------------------------------
+# clocks during the timed region (NVML polled from a thread; nvidia-smi fields)
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle",
+               0x2: "applications_clocks_setting", 0x100: "display_clock_setting"}
+
+    def __init__(self, torch_device_index: int, period_s: float = 0.01):
+        self.period = period_s
+        self.samples = []
+        self.err = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml as nv
+            import torch
+            nv.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(torch_device_index).uuid)
+            try:
+                self.h = nv.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:  # noqa: BLE001 — older bindings want bytes
+                self.h = nv.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self.nv = nv
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self.err = f"nvml unavailable: {e}"
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                pw = nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((sm, rs, pw))
+            except Exception as e:  # noqa: BLE001
+                self.err = str(e)
+                return
+            time.sleep(self.period)
+
+    def start(self):
+        if self.err is None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        if self.err and not self.samples:
+            return {"error": self.err}
+        sms = [s[0] for s in self.samples]
+        mask = 0
+        for s in self.samples:
+            mask |= s[1]
+        reasons = sorted({n for b, n in self.REASONS.items() if mask & b and n != "gpu_idle"})
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sms),
+                "power_w_max": max((s[2] for s in self.samples), default=None),
+                "source": "nvml (nvidia-smi clocks.sm / clocks_event_reasons)"}
+
+
+# ----------------------------------------------------------------------------------------
+# CPU baseline (oracle port on the host cores) — also the reference arm
+# ----------------------------------------------------------------------------------------
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
+
+
+def cpu_step_factory(w, target_s: float):
+    """A callable doing one bounded sample of the workload on the CPU, its work units, and a
+    description of the sample. The sample is sized so one call takes about target_s."""
+    import numpy as np
+    g = np.random.default_rng(w["seed"])
+    if w["kind"] == "gemm":
+        N, K = w["N"], w["K"]
+        integer = w["ab"] == "Int8"
+        B = (g.integers(-128, 128, size=(K, N)).astype(np.float64) if integer
+             else g.uniform(-1, 1, size=(K, N)).astype(np.float16).astype(np.float32))
+        rows = 64
+        while True:
+            A = (g.integers(-128, 128, size=(rows, K)).astype(np.float64) if integer
+                 else g.uniform(-1, 1, size=(rows, K)).astype(np.float16).astype(np.float32))
+            t0 = time.perf_counter()
+            A @ B
+            dt = time.perf_counter() - t0
+            if dt >= target_s / 2 or rows >= w["M"]:
+                break
+            rows = min(w["M"], rows * 2)
+        how = ("exact int8 GEMM as float64 BLAS (integer partial sums < 2^53)" if integer
+               else "float32 BLAS sgemm on fp16-rounded inputs")
+        sample = f"{rows} of {w['M']} rows of A: ({rows}x{K}) @ ({K}x{N}), {how}"
+        return (lambda: A @ B), 2.0 * rows * N * K, sample
+    # attention: whole (b, h) units at full sequence length
+    from oracle.attention import attention_blockwise
+    S, D = w["S"], w["D"]
+    q = g.standard_normal((S, D), dtype=np.float32)
+    k = g.standard_normal((S, D), dtype=np.float32)
+    v = g.standard_normal((S, D), dtype=np.float32)
+    units = 1
+    per = 4.0 * S * S * D / (2 if w["causal"] else 1)
+    t0 = time.perf_counter()
+    attention_blockwise(q, k, v, w["causal"], D ** -0.5, block=512)
+    dt = time.perf_counter() - t0
+    units = max(1, min(int(target_s / max(dt, 1e-3)), w["B"] * w["Hq"]))
+
+    def step():
+        for _ in range(units):
+            attention_blockwise(q, k, v, w["causal"], D ** -0.5, block=512)
+    sample = (f"{units} of {w['B'] * w['Hq']} (batch, head) units at S={S}, D={D}, "
+              "blockwise float32 online softmax on host BLAS")
+    return step, units * per, sample
+
+
+def cpu_baseline(w, budget_s: float = 12.0):
+    step, units, sample = cpu_step_factory(w, target_s=min(3.0, budget_s / 4))
+    step()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
+    return {"value": units / best / 1e12, "unit": unit, "cores": blas_threads(), "kind": "port",
+            "sample": sample + f"; best of {len(times)} runs", "host_cpus": os.cpu_count()}
+
+
+def run_reference(args, w):
+    step, units, sample = cpu_step_factory(w, target_s=1.0)
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    value = units * len(times) / tot / 1e12
+    unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": tot / len(times) * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic (seeded)",
+        "config": config_of(w, args.gpus, reference=True),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": blas_threads(), "kind": "port",
+                         "sample": sample, "host_cpus": os.cpu_count()},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("Lava's own path (Julia -> SPIR-V on lavapipe, host Julia BLAS) is unavailable "
+                 "on this box (no Julia, no graphics stack); the oracle port stands in"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_of(w, n, reference=False):
+    c = {"workload": f"{w['cfg']} " + (
+        f"{w['ab']} GEMM M={w['M']} N={w['N']} K={w['K']} per GPU, {w['out']} C, A row-major, "
+        f"B column-major, C column-major" if w["kind"] == "gemm" else
+        f"{w['ab']} flash-attention fwd B={w['B']} Hq={w['Hq']} Hkv={w['Hkv']} S={w['S']} "
+        f"D={w['D']} causal={w['causal']} per GPU")}
+    c["parallelism"] = (f"row-shard x{n} (independent shards, no collective)" if w["kind"] == "gemm"
+                        else f"(batch, kv-head) shard x{n}") if n > 1 else "single GPU"
+    c["l2"] = "inputs larger than L2 (126 MB): working set re-read every step from HBM"
+    if reference:
+        c["device"] = "host CPU"
+    return c
+
+
+# ----------------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------------
+def make_gemm(torch, lvb, w, rank):
+    gen = torch.Generator(device="cuda").manual_seed(w["seed"] * 1000 + rank)
+    M, N, K = w["M"], w["N"], w["K"]
+    tdt = {"Float16": torch.float16, "BFloat16": torch.bfloat16, "Int8": torch.int8}[w["ab"]]
+    odt = {"Float16": torch.float16, "BFloat16": torch.bfloat16, "Float32": torch.float32,
+           "Int32": torch.int32}[w["out"]]
+    if tdt == torch.int8:
+        A = torch.randint(-128, 128, (M, K), generator=gen, device="cuda", dtype=torch.int16).to(tdt)
+        Bs = torch.randint(-128, 128, (N, K), generator=gen, device="cuda", dtype=torch.int16).to(tdt)
+    else:
+        A = (torch.rand((M, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
+        Bs = (torch.rand((N, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
+    Cs = torch.empty((N, M), dtype=odt, device="cuda")        # column-major C storage
+    B, C = Bs.t(), Cs.t()
+
+    def step():
+        lvb.gemm(C, A, B)
+    ins, outs = [A, Bs], [Cs]
+
+    def step_e2e(h_ins, h_outs):
+        A.copy_(h_ins[0], non_blocking=True)
+        Bs.copy_(h_ins[1], non_blocking=True)
+        lvb.gemm(C, A, B)
+        h_outs[0].copy_(Cs, non_blocking=True)
+    return step, step_e2e, ins, outs
+
+
+def make_attn(torch, lvb, w, rank):
+    gen = torch.Generator(device="cuda").manual_seed(w["seed"] * 1000 + rank)
+    tdt = {"Float16": torch.float16, "BFloat16": torch.bfloat16}[w["ab"]]
+    Bn, Hq, Hkv, S, D = w["B"], w["Hq"], w["Hkv"], w["S"], w["D"]
+    Q = torch.randn((Bn, Hq, S, D), generator=gen, device="cuda").to(tdt)
+    K = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(tdt)
+    V = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(tdt)
+    O = torch.empty_like(Q)
+
+    def step():
+        lvb.attention(O, Q, K, V, causal=w["causal"])
+
+    def step_e2e(h_ins, h_outs):
+        Q.copy_(h_ins[0], non_blocking=True)
+        K.copy_(h_ins[1], non_blocking=True)
+        V.copy_(h_ins[2], non_blocking=True)
+        lvb.attention(O, Q, K, V, causal=w["causal"])
+        h_outs[0].copy_(O, non_blocking=True)
+    return step, step_e2e, [Q, K, V], [O]
+
+
+def run_gpu(args, w):
+    import torch
+    import torch.distributed as dist
+    import importlib.util
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+
+    spec = importlib.util.spec_from_file_location("lvb_build", PKG / "build.py")
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    if rank == 0:
+        b.build()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    import lvb
+
+    step, step_e2e, ins, outs = (make_gemm if w["kind"] == "gemm" else make_attn)(torch, lvb, w, rank)
+    units = work_units(w)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing ----
+    for _ in range(args.warmup):
+        step()
+    st = lvb.device_status()
+    assert st[0] == 0, f"device status {st} after warm-up"
+    barrier()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    clocks = sampler.stop()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    barrier()
+    st = lvb.device_status()
+    assert st[0] == 0, f"device status {st} after the timed region"
+    ms = max_over_ranks(ms_local)
+    value = units * world / (ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers ----
+    h_ins = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
+    h_outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+    for h, t in zip(h_ins, ins):
+        h.copy_(t)
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        step_e2e(h_ins, h_outs)
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        step_e2e(h_ins, h_outs)
+    e1.record(stream)
+    e1.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    barrier()
+    h2d = sum(t.numel() * t.element_size() for t in ins)
+    d2h = sum(t.numel() * t.element_size() for t in outs)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w)
+
+    if rank == 0:
+        peaks, src = measured_peaks()
+        peak = peaks["bf16_tflops"]
+        unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
+        if w["ab"] == "Int8":
+            # no measured int8 peak: dense int8 is twice dense bf16 on this part
+            peak = 2 * peak
+            src += " (2x bf16 burst: int8 dense rate)"
+        achieved = units / (ms_local * 1e-3) / 1e12
+        traffic = profile_traffic(args.workload)
+        line = {
+            "impl": "lvb", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": w["dtype"], "data": "synthetic: seeded torch RNG, shapes/distributions of "
+            f"BASELINE {w['cfg']}",
+            "config": config_of(w, world),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{src} burst bf16_tflops (MEASURED_PEAKS.json)"
+                         if src.startswith("measured") else f"{src} 1.59 PFLOP/s"},
+            "e2e": {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "steps": e2e_steps,
+                    "path": "lvb Python binding -> liblvb C ABI; pinned host buffers; "
+                            "H2D inputs + kernel + D2H output per step"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gemm_f16", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="lvb", choices=["lvb", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    if args.steps is None:
+        # about 2 s of timed device work at the expected rate
+        args.steps = {"gemm_f16": 2000, "gemm_f16_512": 2000, "gemm_i8": 3000,
+                      "gemm_bf16": 250, "attn_f16": 2000, "attn_bf16": 40}[args.workload]
+        if args.impl == "reference":
+            args.steps = 5
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        run_reference(args, w)
+        return 0
+    run_gpu(args, w)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

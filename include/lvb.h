@@ -1,0 +1,198 @@
+/*
+ * lvb.h — C ABI of liblvb, the B200 (sm_100a) backend for the cooperative-matrix GEMM and
+ * flash-attention path of Lava.jl.
+ *
+ * Lava.jl is a compiler: a kernel author writes a GEMM or attention kernel against its
+ * device vocabulary (CoopMatrix / AcceleratedMatrix / WorkgroupMatrix, coopmat_load,
+ * muladd, convert, copyto!, coopmat_reduce, coopmat_perelement, tensor_load with clamp),
+ * Lava lowers it to SPIR-V and a Vulkan runtime dispatches it. This library replaces that
+ * execution path for the two ops that vocabulary exists to serve: every entry point below
+ * is what a host package binds with `ccall` in place of compiling and dispatching a
+ * coopmat kernel. The reference interface each one stands in for is cited beside it
+ * (paths relative to the Lava.jl source tree).
+ *
+ * Conventions
+ *  - Plain pointers and sizes; device pointers are CUDA device addresses, `stream` is a
+ *    cudaStream_t / CUstream (NULL = the legacy default stream).
+ *  - Every entry point returns an lvb_status. On failure lvb_last_error() returns a
+ *    thread-local message of the form "<operation>: <message> (<suggestion>)", the triad
+ *    of Lava's LavaError (src/runtime/errors.jl:4-24).
+ *  - Work is enqueued on the caller's stream and returns without synchronising. A device
+ *    side failure (a bounded wait that expired) is recorded in a per-device status word
+ *    that lvb_device_status() reads, like Lava's exception flag word that the host checks
+ *    at the next synchronisation (src/compiler/entry_wrapper.jl:9-11,199-216).
+ *  - The library never frees caller memory and holds no pointer past a call.
+ */
+#ifndef LVB_H
+#define LVB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LVB_ABI_VERSION 1
+
+typedef enum lvb_status {
+  LVB_OK = 0,
+  LVB_ERR_INVALID_ARG = 1, /* a null pointer, a negative size, a leading dimension too small */
+  LVB_ERR_UNSUPPORTED = 2, /* a legal request this build does not implement (dtype pair, layout, alignment) */
+  LVB_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  LVB_ERR_TIMEOUT = 4,     /* a kernel's bounded wait expired (read through lvb_device_status) */
+  LVB_ERR_NCCL = 5,        /* NCCL missing or a collective failed */
+  LVB_ERR_NO_DEVICE = 6    /* no sm_100 device visible */
+} lvb_status;
+
+/* Component types. Lava's coopmat component types are Float16, Float32, Int8, UInt8,
+ * Int32, UInt32 (src/device/coopmat_intrinsics.jl:16-19); BFloat16 is added for B200. */
+typedef enum lvb_dtype {
+  LVB_F16 = 0,
+  LVB_BF16 = 1,
+  LVB_F32 = 2,
+  LVB_I8 = 3,
+  LVB_U8 = 4,
+  LVB_I32 = 5,
+  LVB_U32 = 6
+} lvb_dtype;
+
+/* Matrix scopes (src/vocabulary/matrix.jl:60-66). */
+typedef enum lvb_scope { LVB_SUBGROUP_SCOPE = 0, LVB_WORKGROUP_SCOPE = 1 } lvb_scope;
+
+/* ---------------------------------------------------------------------------------------
+ * Capabilities — the answer a backend gives to Lava.caps(backend) (src/vocabulary/caps.jl:
+ * 54-65, 120) and to matrix_shapes / supports / bestshape (caps.jl:158-169,
+ * src/vocabulary/matrix.jl:88-172).
+ * ------------------------------------------------------------------------------------- */
+typedef struct lvb_matrix_shape {
+  int32_t ab;    /* lvb_dtype of A and B */
+  int32_t acc;   /* lvb_dtype of the accumulator */
+  int32_t M, N, K;
+  int32_t scope; /* lvb_scope */
+} lvb_matrix_shape;
+
+typedef struct lvb_device_caps {
+  int32_t coopmat;          /* matrix multiply-add usable at all */
+  int32_t tile;             /* square fp16->fp32 instruction extent */
+  int32_t subgroup;         /* lanes per subgroup (warp) */
+  int32_t coopmatsubgroup;  /* subgroup width a matrix kernel gets */
+  int64_t sharedbudget;     /* bytes of workgroup-shared memory per workgroup */
+  int32_t workgrouplimit;   /* threads per workgroup */
+  int32_t cores;            /* SMs */
+  int32_t warps;            /* max resident subgroups per SM */
+  int32_t n_wggran;         /* rows used in wggran */
+  int32_t wggran[8][4];     /* (invocations, M, N, K) workgroup-scope granularity rows */
+  int32_t n_shapes;         /* number of subgroup-scope shapes lvb_matrix_shapes reports */
+  int32_t cc_major, cc_minor;
+} lvb_device_caps;
+
+/* Static caps of a B200 (sm_100a) — host only, needs no GPU. Used by lvb_caps and by tests
+ * that check a tiling decision on a machine without the device (caps.jl:84-108). */
+int lvb_caps_sm100(lvb_device_caps* out);
+/* Caps of CUDA device `device`: the sm_100a table with the live SM count / shared budget.
+ * Returns LVB_ERR_NO_DEVICE when the device is absent or not sm_100. */
+int lvb_caps(int device, lvb_device_caps* out);
+/* The subgroup-scope shape table (matrix_shapes, caps.jl:158-159). Writes up to
+ * `capacity` entries and the total count to *count. Host only. */
+int lvb_matrix_shapes(lvb_matrix_shape* out, int32_t capacity, int32_t* count);
+/* bestshape (matrix.jl:155-172): squarest, then largest, among shapes with ab/acc/scope.
+ * Returns LVB_ERR_UNSUPPORTED when the table has none (Lava's `nothing`). Host only. */
+int lvb_bestshape(int32_t ab, int32_t acc, int32_t scope, lvb_matrix_shape* out);
+
+/* ---------------------------------------------------------------------------------------
+ * GEMM: C = A·B with accumulation in C's element type, as coopmat_muladd does
+ * (src/vocabulary/coopmat.jl:190-203; src/device/coopmat_intrinsics.jl:303-320), loads and
+ * stores with Lava's addressing — `stride` elements between rows (row-major, Val(true)) or
+ * columns (column-major) (coopmat.jl:124-161; coopmat_intrinsics.jl:57-75,179-218) — and
+ * the fp32 -> fp16/bf16 conversion of `convert` (round to nearest even; coopmat.jl:178-182)
+ * fused into the store. Ragged edges follow TENSOR_CLAMP_CONSTANT with value 0
+ * (src/vocabulary/tensor.jl:46-51): the tile is computed over zero-filled operands and the
+ * store is clamped to the matrix. Replaces compiling and dispatching a coopmat GEMM kernel
+ * (the loop of test/glsl/coopmat2_gemm_regs.comp:53-83).
+ * ------------------------------------------------------------------------------------- */
+typedef struct lvb_gemm_desc {
+  int32_t a_type, b_type, c_type; /* lvb_dtype */
+  int32_t a_rowmajor;             /* 1: A (M×K) stored row-major (lda >= K) */
+  int32_t b_rowmajor;             /* 0: B (K×N) stored column-major (ldb >= K) */
+  int32_t c_rowmajor;             /* 0: C (M×N) column-major (ldc >= M); 1: row-major (ldc >= N) */
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;          /* elements */
+} lvb_gemm_desc;
+
+/* The tiling the library will use for a descriptor (host only, no GPU). */
+typedef struct lvb_gemm_plan {
+  int32_t swap_ab;      /* 1: computed as Cᵀ = Bᵀ·Aᵀ so the store is lane-contiguous */
+  int32_t tile_m, tile_n, tile_k;
+  int32_t stages;
+  int32_t tiles;        /* output tiles */
+  int32_t ctas;         /* persistent CTAs launched (<= SM count) */
+  int32_t smem_bytes;   /* dynamic shared memory per CTA */
+  int32_t tmem_cols;    /* TMEM columns allocated per CTA */
+  int32_t instr_m, instr_n, instr_k; /* tcgen05.mma shape */
+} lvb_gemm_plan;
+
+/* Validate a descriptor (host only). */
+int lvb_gemm_check(const lvb_gemm_desc* d);
+/* Validate and plan for `sm_count` SMs (host only). */
+int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* out);
+/* Enqueue C = A·B on `stream` (on the current CUDA device). Supported pairs:
+ *   F16×F16 -> F32|F16|BF16,  BF16×BF16 -> F32|F16|BF16,  I8×I8 -> I32,  U8×U8 -> U32.
+ * A row-major and B column-major (both K-contiguous); C either layout. A and B must start
+ * on 16-byte boundaries with lda·sizeof, ldb·sizeof multiples of 16 bytes. */
+int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Flash-attention forward: O = softmax(scale·Q·Kᵀ + mask)·V per (batch, query head), fp32
+ * online softmax, P converted to the input type for the second product — the key-block
+ * loop a Lava flash kernel writes with coopmat_muladd, coopmat_reduce(max/+, Row),
+ * coopmat_perelement(exp) and coopmat_convert (src/device/coopmat_intrinsics.jl:520-755;
+ * src/compiler/spirv/coopmat.jl:783-822,887-991). GQA: query head h reads KV head
+ * h / (heads_q / heads_kv). Causal: query i sees keys j <= i + (seq_kv - seq_q).
+ * Tensors are [batch][head][seq][head_dim] with head_dim contiguous — Lava's (E, L, H, B)
+ * column-major arrays (src/device/sharedmemory.jl:73-76).
+ * ------------------------------------------------------------------------------------- */
+typedef struct lvb_attn_desc {
+  int32_t dtype;      /* LVB_F16 or LVB_BF16 for Q, K, V and O */
+  int32_t causal;
+  int64_t batch, heads_q, heads_kv, seq_q, seq_kv, head_dim;
+  float scale;        /* usually 1/sqrt(head_dim) */
+  int32_t reserved;
+  /* element strides of batch, head and seq; 0 for all three of a tensor = packed */
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3];
+} lvb_attn_desc;
+
+int lvb_attention_check(const lvb_attn_desc* d);
+/* Enqueue the forward pass. `lse` (nullable) receives the fp32 natural-log row
+ * log-sum-exp of scale·QKᵀ, laid out [batch][heads_q][seq_q]. */
+int lvb_attention_fwd(const lvb_attn_desc* d, const void* Q, const void* K, const void* V,
+                      void* O, float* lse, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Runtime helpers for host packages that own device buffers (Lava leaves these to its
+ * runtime; LavaDeviceArray is a non-owning (ptr, dims) value, src/device/devicearray.jl:
+ * 25-38).
+ * ------------------------------------------------------------------------------------- */
+int lvb_abi_version(void);
+const char* lvb_last_error(void);
+const char* lvb_status_string(int status);
+int lvb_device_count(int32_t* n);
+int lvb_set_device(int device);
+int lvb_malloc(void** ptr, size_t bytes);
+int lvb_free(void* ptr);
+int lvb_memcpy_htod(void* dst, const void* src, size_t bytes, void* stream);
+int lvb_memcpy_dtoh(void* dst, const void* src, size_t bytes, void* stream);
+int lvb_stream_create(void** stream);
+int lvb_stream_destroy(void* stream);
+int lvb_stream_synchronize(void* stream);
+/* Synchronise `stream`, then read and clear the current device's status word. *code is
+ * LVB_OK or LVB_ERR_TIMEOUT; *where is the wait site, *block the first CTA that gave up. */
+int lvb_device_status(void* stream, int32_t* code, int32_t* where, int32_t* block);
+/* Wall-clock limit of every in-kernel wait, in milliseconds (default 2000; also read from
+ * the environment variable LVB_WAIT_TIMEOUT_MS at first use). */
+int lvb_set_wait_timeout_ms(int64_t ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LVB_H */

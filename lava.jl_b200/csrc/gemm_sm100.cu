@@ -1,0 +1,412 @@
+// gemm_sm100.cu — persistent warp-specialised tcgen05 GEMM for B200 (sm_100a).
+//
+// What it computes is Lava's coopmat GEMM (the k-loop of test/glsl/coopmat2_gemm_regs.comp:
+// 53-83, and the vocabulary path AcceleratedMatrix load -> muladd -> convert -> copyto!,
+// src/vocabulary/coopmat.jl:124-203): D[m,n] = sum_k A[m,k]·B[n,k] accumulated in fp32
+// (kind::f16) or int32 (kind::i8), converted with round-to-nearest-even to the output type
+// and stored with ragged edges clamped.
+//
+// How (kernel space; the host swaps A and B when the caller wants a row-major C):
+//   * operands are K-contiguous ("K-major"); a CTA owns a 128 × BN output tile;
+//   * warp 0 lane 0: TMA producer. Streams 128×128-byte A and BN×128-byte B boxes
+//     (128B swizzle, zero fill past the edges) into a STAGES-deep mbarrier ring;
+//   * warp 1 lane 0: MMA issuer. Four tcgen05.mma (128×BN×16 f16 / ×32 i8) per stage into
+//     one of two TMEM accumulators, tcgen05.commit frees the stage;
+//   * warp 2: allocates / frees TMEM (2·BN columns);
+//   * warps 4-7: epilogue. tcgen05.ld 32 columns at a time; lane = output row, so each
+//     store of one column by a warp writes 32 consecutive m (coalesced, D is m-contiguous);
+//     the accumulator is handed back as soon as it has been read, so the next tile's MMAs
+//     overlap this tile's stores.
+//   * persistent grid (one CTA per SM), tiles visited in groups of GROUP_M row-tiles so the
+//     ~148 tiles in flight share A rows and B columns in L2.
+#include "lvb_internal.h"
+
+namespace lvb {
+
+enum AbKind { AB_F16 = 0, AB_BF16 = 1, AB_S8 = 2, AB_U8 = 3 };
+enum OutKind { OUT_F32 = 0, OUT_F16 = 1, OUT_BF16 = 2, OUT_I32 = 3 };
+
+constexpr int kBM = 128;
+constexpr int kRowBytes = 128;                 // K bytes per stage row (64 f16 / 128 i8)
+constexpr int kAStageBytes = kBM * kRowBytes;  // 16 KB
+constexpr int kThreads = 256;
+constexpr int kGroupM = 16;
+
+struct GemmParams {
+  int M, N, K;            // kernel space
+  int tiles_m, tiles_n, num_kb;
+  int total_tiles;
+  void* D;
+  long long ldd;          // D[m + n*ldd]
+  DevStatus* status;
+  unsigned long long timeout_ns;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kBStageBytes = BN * kRowBytes;
+  static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(p.tiles_m - first_m, kGroupM);
+  const int r = t - g * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+// Wait that ignores the abort flag: used only while draining on the way out.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_ns();
+  while (!bar_try_wait(a, parity)) {
+    if (global_ns() - t0 > timeout_ns) return;
+  }
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_out(void* D, long long idx, uint32_t bits) {
+  if constexpr (OUT == OUT_F32 || OUT == OUT_I32) {
+    reinterpret_cast<uint32_t*>(D)[idx] = bits;
+  } else if constexpr (OUT == OUT_F16) {
+    reinterpret_cast<__half*>(D)[idx] = __float2half_rn(__uint_as_float(bits));
+  } else {
+    reinterpret_cast<__nv_bfloat16*>(D)[idx] = __float2bfloat16_rn(__uint_as_float(bits));
+  }
+}
+
+template <int AB, int OUT, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
+  constexpr int kElemsPerRow = kInt ? 128 : 64;  // K elements per stage
+  constexpr int kMmaK = kInt ? 32 : 16;          // K per tcgen05.mma
+  constexpr int kMmasPerStage = kElemsPerRow / kMmaK;  // 4
+  constexpr uint32_t kDescStep = (kMmaK * (kInt ? 1 : 2)) >> 4;  // 32 bytes -> 2
+  constexpr uint32_t kIdesc =
+      kInt ? make_idesc(2, AB == AB_S8 ? 1 : 0, AB == AB_S8 ? 1 : 0, 0, 0, kBM, BN)
+           : make_idesc(1, AB == AB_BF16 ? 1 : 0, AB == AB_BF16 ? 1 : 0, 0, 0, kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * kAStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;            // [S]  TMA -> MMA
+  uint64_t* empty = bars + S;       // [S]  MMA -> TMA
+  uint64_t* tfull = bars + 2 * S;   // [2]  MMA -> epilogue
+  uint64_t* tempty = tfull + 2;     // [2]  epilogue -> MMA
+  uint64_t* drain = tempty + 2;     // [1]  MMA drain on exit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&tfull[b], 1);
+      bar_init(&tempty[b], 128);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t filled_mask = 0;       // stages filled at least once
+    uint32_t last_phase[8] = {0};
+    bool ok = true;
+    const uint64_t pol_a = policy_evict_last();
+    const uint64_t pol_b = policy_evict_last();
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!wait_bar(&empty[stage], phase ^ 1, g, 1, t)) { ok = false; break; }
+        bar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+        tma_load_2d_hint(sA + stage * kAStageBytes, &tmA, kb * kElemsPerRow, tm * kBM,
+                         &full[stage], pol_a);
+        tma_load_2d_hint(sB + stage * Cfg::kBStageBytes, &tmB, kb * kElemsPerRow, tn * BN,
+                         &full[stage], pol_b);
+        filled_mask |= 1u << stage;
+        last_phase[stage] = phase;
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) {
+      // Let every copy this thread started land before the CTA's shared memory goes away.
+      for (int s = 0; s < S; ++s)
+        if (filled_mask & (1u << s)) drain_wait(&full[s], last_phase[s], p.timeout_ns);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    const uint32_t a_base = smem_u32(sA);
+    const uint32_t b_base = smem_u32(sB);
+    for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 2, t)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!wait_bar(&full[stage], phase, g, 3, t)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t adesc = sdesc_sw128(a_base + stage * kAStageBytes, 16, 1024);
+        const uint64_t bdesc = sdesc_sw128(b_base + stage * Cfg::kBStageBytes, 16, 1024);
+#pragma unroll
+        for (int k = 0; k < kMmasPerStage; ++k) {
+          const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+          if constexpr (kInt)
+            mma_i8_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+          else
+            mma_f16_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+        }
+        mma_commit(&empty[stage]);
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      mma_commit(&tfull[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    // Every MMA this thread issued has finished before TMEM is released.
+    mma_commit(drain);
+    drain_wait(drain, 0, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 4;             // TMEM lanes 32*ew .. 32*ew+31
+    const int row = ew * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      if (!wait_bar(&tfull[acc], acc_phase, g, 4, t)) break;
+      tc_fence_after();
+      const int m = tm * kBM + row;
+      const bool m_ok = m < p.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * BN;
+      uint32_t r[32];
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the predicated stores
+        tmem_ld32(t_row + c * 32, r);
+        tmem_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          bar_arrive(&tempty[acc]);  // accumulator fully read: hand it back
+        }
+        if (p.num_kb == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        const int n0 = tn * BN + c * 32;
+        if (m_ok) {
+          if (n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+          }
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------------------
+namespace {
+
+int ab_kind_of(int dt) {
+  switch (dt) {
+    case LVB_F16: return AB_F16;
+    case LVB_BF16: return AB_BF16;
+    case LVB_I8: return AB_S8;
+    case LVB_U8: return AB_U8;
+  }
+  return -1;
+}
+int out_kind_of(int dt) {
+  switch (dt) {
+    case LVB_F32: return OUT_F32;
+    case LVB_F16: return OUT_F16;
+    case LVB_BF16: return OUT_BF16;
+    case LVB_I32:
+    case LVB_U32: return OUT_I32;
+  }
+  return -1;
+}
+
+template <int AB, int OUT, int BN>
+int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int ctas,
+             cudaStream_t stream, DeviceState* dev) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<AB, OUT, BN>;
+  // The attribute is per function and per device; setting it every call is cheap and
+  // keeps this thread-safe without a cache.
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+  kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "kernel launch");
+  return LVB_OK;
+}
+
+template <int AB, int OUT>
+int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+              int ctas, cudaStream_t s, DeviceState* dev) {
+  switch (bn) {
+    case 256: return launch_t<AB, OUT, 256>(ta, tb, p, ctas, s, dev);
+    case 128: return launch_t<AB, OUT, 128>(ta, tb, p, ctas, s, dev);
+    case 64: return launch_t<AB, OUT, 64>(ta, tb, p, ctas, s, dev);
+  }
+  return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "tile width not built");
+}
+
+}  // namespace
+
+int gemm_smem_bytes(int bn) {
+  switch (bn) {
+    case 256: return GemmCfg<256>::kSmemBytes;
+    case 128: return GemmCfg<128>::kSmemBytes;
+    case 64: return GemmCfg<64>::kSmemBytes;
+  }
+  return 0;
+}
+int gemm_stages(int bn) {
+  switch (bn) {
+    case 256: return GemmCfg<256>::kStages;
+    case 128: return GemmCfg<128>::kStages;
+    case 64: return GemmCfg<64>::kStages;
+  }
+  return 0;
+}
+
+// K == 0: C = 0 (the empty sum), written through the same clamped addressing.
+__global__ void gemm_zero_kernel(uint8_t* C, long long rows, long long cols, long long ld,
+                                 int esize) {
+  const long long total = rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i % rows, c = i / rows;
+    uint8_t* p = C + (c * ld + r) * esize;
+    for (int b = 0; b < esize; ++b) p[b] = 0;
+  }
+}
+
+int gemm_zero_fill(const lvb_gemm_desc* d, void* C, cudaStream_t stream) {
+  // Lane-contiguous dimension first: column-major C has M contiguous, row-major N.
+  const long long rows = d->c_rowmajor ? d->N : d->M;
+  const long long cols = d->c_rowmajor ? d->M : d->N;
+  const int es = dtype_size(d->c_type);
+  const long long total = rows * cols;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+  gemm_zero_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<uint8_t*>(C), rows, cols, d->ldc,
+                                               es);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LVB_OK : fail_cuda(e, "lvb_gemm", "zero-fill launch");
+}
+
+int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A, const void* B,
+                void* C, cudaStream_t stream, DeviceState* dev) {
+  const int esize = dtype_size(d->a_type);
+  // Kernel space: rows of "A" are the lane (contiguous-store) dimension.
+  const void* kA = plan.swap_ab ? B : A;
+  const void* kB = plan.swap_ab ? A : B;
+  const int64_t kM = plan.swap_ab ? d->N : d->M;
+  const int64_t kN = plan.swap_ab ? d->M : d->N;
+  const int64_t ldka = plan.swap_ab ? d->ldb : d->lda;
+  const int64_t ldkb = plan.swap_ab ? d->lda : d->ldb;
+  const uint32_t box_k = 128 / esize;
+
+  CUtensorMap ta, tb;
+  int st = make_tmap_2d(&ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka, box_k,
+                        kBM, "lvb_gemm");
+  if (st) return st;
+  st = make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
+                    (uint32_t)plan.tile_n, "lvb_gemm");
+  if (st) return st;
+
+  GemmParams p;
+  p.M = (int)kM;
+  p.N = (int)kN;
+  p.K = (int)d->K;
+  p.tiles_m = (int)((kM + kBM - 1) / kBM);
+  p.tiles_n = (int)((kN + plan.tile_n - 1) / plan.tile_n);
+  p.num_kb = (int)((d->K + box_k - 1) / box_k);
+  p.total_tiles = p.tiles_m * p.tiles_n;
+  p.D = C;
+  p.ldd = d->ldc;
+  p.status = dev->status;
+  p.timeout_ns = wait_timeout_ns();
+
+  const int ab = ab_kind_of(d->a_type);
+  const int out = out_kind_of(d->c_type);
+  const int bn = plan.tile_n;
+  const int ctas = plan.ctas;
+  if (ab == AB_F16) {
+    if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_F16) return launch_bn<AB_F16, OUT_F16>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_BF16) return launch_bn<AB_F16, OUT_BF16>(bn, ta, tb, p, ctas, stream, dev);
+  } else if (ab == AB_BF16) {
+    if (out == OUT_F32) return launch_bn<AB_BF16, OUT_F32>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_F16) return launch_bn<AB_BF16, OUT_F16>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_BF16) return launch_bn<AB_BF16, OUT_BF16>(bn, ta, tb, p, ctas, stream, dev);
+  } else if (ab == AB_S8 && out == OUT_I32) {
+    return launch_bn<AB_S8, OUT_I32>(bn, ta, tb, p, ctas, stream, dev);
+  } else if (ab == AB_U8 && out == OUT_I32) {
+    return launch_bn<AB_U8, OUT_I32>(bn, ta, tb, p, ctas, stream, dev);
+  }
+  return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "dtype combination not built");
+}
+
+}  // namespace lvb

@@ -1,0 +1,63 @@
+// lvb_internal.h — host-side plumbing shared by the translation units of liblvb.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/lvb.h"
+#include "sm100.cuh"
+
+namespace lvb {
+
+// Thread-local error message; returns `status` so call sites can `return fail(...)`.
+int fail(int status, const std::string& op, const std::string& msg, const std::string& hint = "");
+int fail_cuda(cudaError_t e, const std::string& op, const char* what);
+void clear_error();
+
+// Per-device state, created on first use with the device current.
+struct DeviceState {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  size_t smem_optin = 0;
+  DevStatus* status = nullptr;   // device status word (cudaMalloc'd once per device)
+};
+// Returns nullptr (and sets the error) when the current device is unusable.
+DeviceState* current_device_state(const char* op);
+
+uint64_t wait_timeout_ns();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+// 2-D map over a K-contiguous (or generally inner-contiguous) matrix of `rows` rows of
+// `inner` elements, leading dimension `ld` elements, elements of `esize` bytes, box
+// `box_inner` × `box_rows`, 128-byte swizzle. Returns 0 or an lvb_status.
+int make_tmap_2d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
+                 uint64_t ld, uint32_t box_inner, uint32_t box_rows, const char* op);
+
+// 3-D map [outer][rows][inner] with element strides (ld_rows, ld_outer).
+int make_tmap_3d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
+                 uint64_t outer, uint64_t ld_rows, uint64_t ld_outer, uint32_t box_inner,
+                 uint32_t box_rows, const char* op);
+
+int dtype_size(int dt);
+const char* dtype_name(int dt);
+
+// ---- GEMM (gemm_sm100.cu) ----
+struct GemmKernelArgs;
+int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
+                const void* B, void* C, cudaStream_t stream, DeviceState* dev);
+
+// ---- attention (attn_sm100.cu) ----
+int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,
+                float* lse, cudaStream_t stream, DeviceState* dev);
+
+}  // namespace lvb

@@ -1,0 +1,114 @@
+"""GEMM oracle — TEST INFRASTRUCTURE (see ``oracle/__init__.py``; parity unpinned).
+
+Two restatements of Lava's coopmat GEMM:
+
+* ``gemm_tiled`` — the algorithm of ``test/glsl/coopmat2_gemm_regs.comp:53-83``: one
+  BM×BN workgroup accumulator per output tile, the k-loop stepping BK, A and B slices read
+  through clamp-constant(0) tensor layouts, ``coopMatMulAdd`` into an fp32 (int32)
+  accumulator, conversion to the output type, clamped tensor store. Small sizes only.
+* ``gemm_ref`` — the same product as one float64 (int64) matmul, rounded once to the output
+  type: the value every correct kernel approximates. Used at all sizes.
+
+For fp16/bf16 inputs each product a·b is exact in float64 (11+11 or 8+8 significant bits)
+and so are sums of up to 2^(53-22-2·e) such terms of bounded range; the tests use that to
+check ``gemm_ref`` bit for bit against exact rational arithmetic on small cases.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from .vocab import (coopmat_convert, coopmat_muladd, tensor_load_clamped,
+                    tensor_store_clamped, round_bf16)
+
+FLOAT_OUT = ("Float32", "Float16", "BFloat16")
+
+
+def to_float64(x: np.ndarray, T: str) -> np.ndarray:
+    """Values of a matrix stored as T (bf16 given as float32 values or uint16 bits)."""
+    if T == "BFloat16" and x.dtype == np.uint16:
+        from .vocab import bf16_bits_to_f32
+        return bf16_bits_to_f32(x).astype(np.float64)
+    return np.asarray(x).astype(np.float64)
+
+
+def gemm_ref(A: np.ndarray, B: np.ndarray, out: str) -> np.ndarray:
+    """C = A·B with A (M,K), B (K,N) given as numpy arrays of their stored VALUES
+    (float16 / float32-holding-bf16-values / int8 / uint8).
+
+    Floats: float64 accumulation, one RNE rounding to ``out``; returns float32 for
+    Float32, float16 for Float16, float32 holding bf16 values for BFloat16.
+    Integers: exact int64 accumulation; returns int32 / uint32 and asserts the result fits
+    (Lava's integer muladd accumulates in the accumulator's 32-bit type,
+    src/compiler/spirv/coopmat.jl:112-151)."""
+    if np.issubdtype(A.dtype, np.integer):
+        acc = A.astype(np.int64) @ B.astype(np.int64)
+        dt = np.int32 if out == "Int32" else np.uint32
+        info = np.iinfo(dt)
+        assert acc.size == 0 or (acc.min() >= info.min and acc.max() <= info.max), "overflow"
+        return acc.astype(dt)
+    acc = A.astype(np.float64) @ B.astype(np.float64)
+    return coopmat_convert(acc, out)
+
+
+def gemm_tiled(A: np.ndarray, B: np.ndarray, out: str, BM: int = 128, BN: int = 128,
+               BK: int = 64) -> np.ndarray:
+    """The workgroup-tile algorithm of coopmat2_gemm_regs.comp (see module doc)."""
+    M, K = A.shape
+    _, N = B.shape
+    integer = np.issubdtype(A.dtype, np.integer)
+    if integer:
+        acc_dt = np.int32 if out == "Int32" else np.uint32
+        res = np.zeros((M, N), dtype=acc_dt)
+    else:
+        res = np.zeros((M, N), dtype=np.float32 if out != "Float16" else np.float16)
+    for ir in range(0, M, BM):
+        for ic in range(0, N, BN):
+            s = np.zeros((BM, BN), dtype=np.int32 if integer and out == "Int32" else
+                         (np.uint32 if integer else np.float32))
+            for bk in range(0, K, BK):
+                a = tensor_load_clamped(A, ir, bk, BM, BK)
+                b = tensor_load_clamped(B, bk, ic, BK, BN)
+                s = coopmat_muladd(a, b, s)
+            tile = s if integer else coopmat_convert(s, out)
+            tensor_store_clamped(res, ir, ic, tile)
+    return res
+
+
+def rel_frobenius(x: np.ndarray, ref: np.ndarray) -> float:
+    x = np.asarray(x, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    den = np.linalg.norm(ref)
+    return float(np.linalg.norm(x - ref) / den) if den > 0 else float(np.linalg.norm(x))
+
+
+def max_abs(x: np.ndarray, ref: np.ndarray) -> float:
+    d = np.abs(np.asarray(x, dtype=np.float64) - np.asarray(ref, dtype=np.float64))
+    return float(d.max()) if d.size else 0.0
+
+
+def ulp_distance_f16(x: np.ndarray, ref: np.ndarray) -> int:
+    """Max distance in fp16 units-in-the-last-place between two float16 arrays."""
+    def key(a):
+        u = np.asarray(a, dtype=np.float16).view(np.uint16).astype(np.int32)
+        return np.where(u & 0x8000, 0x8000 - u, u)   # monotone integer order
+    d = np.abs(key(x) - key(ref))
+    return int(d.max()) if d.size else 0
+
+
+def ulp_distance_bf16(x_vals: np.ndarray, ref_vals: np.ndarray) -> int:
+    """Same for bf16 values carried in float32."""
+    def key(a):
+        u = (np.asarray(a, dtype=np.float32).view(np.uint32) >> 16).astype(np.int32)
+        return np.where(u & 0x8000, 0x8000 - u, u)
+    d = np.abs(key(x_vals) - key(ref_vals))
+    return int(d.max()) if d.size else 0
+
+
+def sgemm_cpu(A32: np.ndarray, B32: np.ndarray) -> np.ndarray:
+    """float32 matmul on the host BLAS (numpy's OpenBLAS) — the stand-in for Lava's
+    reference CPU path (host Julia Float32 matmul, also OpenBLAS)."""
+    return A32 @ B32
+
+
+__all__ = ["gemm_ref", "gemm_tiled", "rel_frobenius", "max_abs", "ulp_distance_f16",
+           "ulp_distance_bf16", "sgemm_cpu", "round_bf16", "to_float64"]

@@ -1,0 +1,167 @@
+"""CPU tier: the C ABI library loads, exports every symbol include/lvb.h declares, and
+answers the host-only questions (caps, shapes, bestshape, argument validation, planning)
+without a GPU — the reference's GPU-free test style (test/runtests.jl:1-20)."""
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "lvb.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(lvb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol(lvb):
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    out = subprocess.run(["nm", "-D", "--defined-only", str(lvb.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r" T (lvb_\w+)", out))
+    missing = [s for s in syms if s not in exported]
+    assert not missing, missing
+    assert sorted(lvb.EXPORTS) == syms          # the Python binding covers the header
+    for s in syms:
+        assert hasattr(lvb.lib, s)
+
+
+def test_library_needs_no_libcuda_at_load(lvb):
+    out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out
+    assert lvb.abi_version() == 1
+
+
+def test_static_caps_answer(lvb):
+    c = lvb.caps()   # static sm_100a table, no GPU
+    assert c.coopmat and c.tile == 16 and c.subgroup == 32 and c.coopmatsubgroup == 32
+    assert c.cores == 148 and c.sharedbudget == 227 * 1024 and c.workgrouplimit == 1024
+    assert lvb.wggranularity(c, 128) == (128, 16, 16)
+    assert lvb.wggranularity(c, 64) is None
+    # `tile` is one entry of `shapes` (caps.jl:84-96)
+    assert lvb.MatrixShape(lvb.F16, lvb.F32, 16, 16, 16) in c.shapes
+
+
+def test_bestshape_squarest_then_largest(lvb):
+    c = lvb.caps()
+    s = lvb.bestshape(c, lvb.F16, lvb.F32)
+    assert (s.M, s.N, s.K) == (16, 16, 16)
+    s = lvb.bestshape(c, lvb.I8, lvb.I32)
+    assert (s.M, s.N, s.K) == (16, 16, 32)
+    assert lvb.bestshape(c, lvb.F32, lvb.F32) is None        # Lava returns `nothing`
+    # The library's own answer agrees, and the workgroup-scope table gives tcgen05 tiles.
+    assert lvb.bestshape_native(lvb.F16, lvb.F32) == lvb.bestshape(c, lvb.F16, lvb.F32)
+    w = lvb.bestshape_native(lvb.BF16, lvb.F32, lvb.WORKGROUP_SCOPE)
+    assert (w.M, w.K) == (128, 16) and w.N in (64, 128, 256)
+    # coopmat=false empties the table but keeps the record (caps.jl:98-108,158-159)
+    import dataclasses
+    off = dataclasses.replace(c, coopmat=False)
+    assert lvb.matrix_shapes(off) == [] and off.shapes
+    assert not lvb.supports(off, lvb.MatrixShape(lvb.F16, lvb.F32, 16, 16, 16))
+
+
+def _desc(lvb, **kw):
+    d = lvb.lvb_gemm_desc(lvb.F16, lvb.F16, lvb.F32, 1, 0, 0, 256, 256, 256, 256, 256, 256)
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+@pytest.mark.parametrize("kw,status,needle", [
+    (dict(M=-1), 1, "negative"),
+    (dict(c_type=5), 2, "no kernel for Float16 x Float16 -> Int32"),
+    (dict(a_type=3, b_type=3, c_type=2), 2, "no kernel"),
+    (dict(a_type=0, b_type=1), 2, "no kernel"),
+    (dict(a_rowmajor=0), 2, "row-major"),
+    (dict(b_rowmajor=1), 2, "row-major"),
+    (dict(lda=100), 1, "lda < K"),
+    (dict(ldb=255), 1, "ldb < K"),
+    (dict(ldc=10), 1, "ldc < M"),
+    (dict(c_rowmajor=1, ldc=10), 1, "ldc < N"),
+    (dict(K=300, lda=300, ldb=304), 2, "16-byte"),
+    (dict(M=2 ** 31), 2, "2^31"),
+])
+def test_gemm_validation(lvb, kw, status, needle):
+    d = _desc(lvb, **kw)
+    st = lvb.lib.lvb_gemm_check(C.byref(d))
+    assert st == status
+    msg = lvb.lib.lvb_last_error().decode()
+    assert needle in msg and msg.startswith("lvb_gemm: ")
+
+
+def test_gemm_null_pointers_rejected_before_device(lvb):
+    d = _desc(lvb)
+    st = lvb.lib.lvb_gemm(C.byref(d), None, None, None, None)
+    assert st == lvb.LVB_ERR_INVALID_ARG
+    with pytest.raises(lvb.LavaError) as e:
+        lvb.check(st)
+    assert e.value.operation == "lvb_gemm" and "NULL" in e.value.message
+    # empty problems are a no-op even without a device
+    d = _desc(lvb, M=0)
+    assert lvb.lib.lvb_gemm(C.byref(d), None, None, None, None) == 0
+
+
+def test_gemm_without_device_fails_loudly(lvb):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    d = _desc(lvb)
+    st = lvb.lib.lvb_gemm(C.byref(d), 256, 256, 256, None)
+    assert st == lvb.LVB_ERR_NO_DEVICE
+    assert "no CUDA device" in lvb.lib.lvb_last_error().decode()
+
+
+def test_plans(lvb):
+    p = lvb.gemm_plan(8192, 8192, 8192, lvb.F16, lvb.F16)
+    assert (p.tile_m, p.tile_n, p.tile_k, p.instr_k) == (128, 256, 64, 16)
+    assert p.tiles == 64 * 32 and p.ctas == 148 and p.swap_ab == 0
+    assert p.tmem_cols == 512 and p.smem_bytes <= 232448
+    q = lvb.gemm_plan(8192, 8192, 8192, lvb.I8, lvb.I32)
+    assert q.tile_k == 128 and q.instr_k == 32
+    r = lvb.gemm_plan(512, 512, 512, lvb.F16, lvb.F32)
+    assert r.tile_n == 64 and r.tiles == 32          # latency-bound size: more CTAs
+    s = lvb.gemm_plan(1000, 300, 64, lvb.F16, lvb.F32, c_rowmajor=True)
+    assert s.swap_ab == 1
+
+
+def test_layout_from_strides(lvb):
+    import torch
+    A = torch.empty(64, 32, dtype=torch.float16)          # row-major (M,K)
+    Bt = torch.empty(48, 32, dtype=torch.float16)         # storage of column-major B
+    Ccol = torch.empty(48, 64, dtype=torch.float32).t()   # column-major (M,N)
+    d = lvb.gemm_desc(Ccol, A, Bt.t())
+    assert (d.a_rowmajor, d.lda, d.b_rowmajor, d.ldb, d.c_rowmajor, d.ldc) == (1, 32, 0, 32, 0, 64)
+    Crow = torch.empty(64, 48, dtype=torch.float32)
+    d = lvb.gemm_desc(Crow, A, Bt.t())
+    assert (d.c_rowmajor, d.ldc) == (1, 48)
+    with pytest.raises(lvb.LavaError):
+        lvb.gemm_desc(Crow, A, torch.empty(33, 48, dtype=torch.float16))
+
+
+def test_attention_validation(lvb):
+    d = lvb.lvb_attn_desc()
+    d.dtype, d.causal = lvb.F16, 1
+    d.batch, d.heads_q, d.heads_kv, d.seq_q, d.seq_kv, d.head_dim = 2, 8, 2, 128, 128, 128
+    d.scale = 0.088
+    assert lvb.lib.lvb_attention_check(C.byref(d)) == 0
+    d.heads_kv = 3
+    assert lvb.lib.lvb_attention_check(C.byref(d)) == lvb.LVB_ERR_INVALID_ARG
+    d.heads_kv = 2
+    d.head_dim = 96
+    assert lvb.lib.lvb_attention_check(C.byref(d)) == lvb.LVB_ERR_UNSUPPORTED
+    d.head_dim = 128
+    d.dtype = lvb.F32
+    assert lvb.lib.lvb_attention_check(C.byref(d)) == lvb.LVB_ERR_UNSUPPORTED
+    d.dtype = lvb.BF16
+    d.scale = float("nan")
+    assert lvb.lib.lvb_attention_check(C.byref(d)) == lvb.LVB_ERR_INVALID_ARG
+
+
+def test_status_strings(lvb):
+    assert lvb.lib.lvb_status_string(4) == b"LVB_ERR_TIMEOUT"
+    assert lvb.lib.lvb_set_wait_timeout_ms(0) == lvb.LVB_ERR_INVALID_ARG

@@ -1,0 +1,214 @@
+"""GPU tier: the tcgen05 GEMM through the C ABI against the oracle.
+
+Tolerances (written here, per the north star):
+  * integer pairs: bit-exact;
+  * Float32 output: relative Frobenius <= 1e-3 and per-element |Δ| <= 1e-2 against the
+    float64 product of the same fp16/bf16 inputs (K <= 8192);
+  * Float16 / BFloat16 output: within 1 unit in the last place of the output type of the
+    float64 product rounded once (one output ulp at |C| ~ 30-100 exceeds 1e-2, so the
+    absolute bound is stated on the Float32-output variant of the same kernel), plus
+    relative Frobenius <= 1e-3 against the unrounded float64 product.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import vocab
+from oracle.gemm import (gemm_ref, rel_frobenius, max_abs, ulp_distance_f16,
+                         ulp_distance_bf16)
+from oracle.inputs import gemm_inputs, GEMM_CONFIGS
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+TNAME = {"Float16": "float16", "BFloat16": "bfloat16", "Float32": "float32", "Int8": "int8",
+         "UInt8": "uint8", "Int32": "int32", "UInt32": "uint32"}
+
+
+def _tdt(torch, T):
+    return getattr(torch, TNAME[T])
+
+
+def to_dev(torch, x, T):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    if T == "BFloat16":
+        t = t.to(torch.bfloat16)       # float32 values that are exact bf16
+    return t.cuda()
+
+
+def run(lvb, torch, A, Bt, ab, out, c_rowmajor=False, lda=None, ldb=None, ldc=None):
+    """A (M,K) and Bt (N,K) storage arrays -> C (M,N) as numpy (float32 for bf16 out)."""
+    M, K = A.shape
+    N = Bt.shape[0]
+    dA = to_dev(torch, A, ab)
+    dB = to_dev(torch, Bt, ab)
+    if lda is not None:     # pad the leading dimension
+        big = torch.zeros(M, lda, dtype=dA.dtype, device="cuda")
+        big[:, :K] = dA
+        dA = big[:, :K]
+    if ldb is not None:
+        big = torch.zeros(N, ldb, dtype=dB.dtype, device="cuda")
+        big[:, :K] = dB
+        dB = big[:, :K]
+    cdt = _tdt(torch, out) if out != "UInt32" else torch.int32
+    if c_rowmajor:
+        w = ldc or N
+        dC = torch.full((M, w), 7, dtype=cdt, device="cuda")[:, :N]
+    else:
+        w = ldc or M
+        dC = torch.full((N, w), 7, dtype=cdt, device="cuda")[:, :M].t()
+    lvb.gemm(dC, dA, dB.t(), c_type=lvb.U32 if out == "UInt32" else None)
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    res = dC.cpu()
+    if out == "BFloat16":
+        return res.float().numpy()
+    if out == "UInt32":
+        return res.numpy().view(np.uint32)
+    return res.numpy()
+
+
+def check(C, A, B, out):
+    ref = gemm_ref(A, B, out)
+    if out in ("Int32", "UInt32"):
+        assert np.array_equal(C, ref)
+        return
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    assert rel_frobenius(C, exact) <= 1e-3
+    if out == "Float32":
+        assert max_abs(C, exact) <= 1e-2
+    elif out == "Float16":
+        assert ulp_distance_f16(C.astype(np.float16), ref) <= 1
+    else:
+        assert ulp_distance_bf16(C, ref) <= 1
+
+
+def test_golden_fixtures(lvb, torch_cuda):
+    torch = torch_cuda
+    files = sorted(f for f in GOLDEN.glob("gemm_*.npz"))
+    assert len(files) >= 6
+    for f in files:
+        z = np.load(f)
+        ab, out = str(z["ab"]), str(z["out"])
+        A, B, Cg = z["A"], z["B"], z["C"]
+        if ab == "BFloat16":
+            A, B = vocab.bf16_bits_to_f32(A), vocab.bf16_bits_to_f32(B)
+        Bt = np.ascontiguousarray(B.T)
+        for crm in (False, True):
+            C = run(lvb, torch, A, Bt, ab, out, c_rowmajor=crm)
+            if out == "BFloat16":
+                C = vocab.f32_to_bf16_bits(C)
+                assert ulp_distance_bf16(vocab.bf16_bits_to_f32(C), vocab.bf16_bits_to_f32(Cg)) <= 1, f.name
+            elif out in ("Int32", "UInt32"):
+                assert np.array_equal(C, Cg), f.name
+            elif out == "Float16":
+                assert ulp_distance_f16(C, Cg) <= 1, f.name
+            else:
+                assert max_abs(C, Cg) <= 1e-5 * max(1.0, np.abs(Cg).max()), f.name
+
+
+def test_config1_fp16_512_fp32(lvb, torch_cuda):
+    cfg = GEMM_CONFIGS["C1"]
+    A, Bt = gemm_inputs(cfg["M"], cfg["N"], cfg["K"], cfg["ab"], cfg["seed"])
+    C = run(lvb, torch_cuda, A, Bt, "Float16", "Float32")
+    check(C, A, Bt.T, "Float32")
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 8), (127, 129, 72), (300, 520, 200),
+                                   (129, 257, 1000), (128, 256, 64), (640, 64, 4096)])
+@pytest.mark.parametrize("ab,out", [("Float16", "Float32"), ("Float16", "Float16"),
+                                    ("BFloat16", "BFloat16"), ("BFloat16", "Float32"),
+                                    ("Float16", "BFloat16")])
+def test_ragged_float(lvb, torch_cuda, M, N, K, ab, out):
+    A, Bt = gemm_inputs(M, N, K, ab, seed=M * 7 + N * 3 + K)
+    for crm in (False, True):
+        C = run(lvb, torch_cuda, A, Bt, ab, out, c_rowmajor=crm)
+        check(C, A, Bt.T, out)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 16), (130, 300, 272), (257, 129, 1040), (512, 512, 8192)])
+@pytest.mark.parametrize("ab,out", [("Int8", "Int32"), ("UInt8", "UInt32")])
+def test_integer_exact(lvb, torch_cuda, M, N, K, ab, out):
+    A, Bt = gemm_inputs(M, N, K, ab, seed=M + N + K)
+    for crm in (False, True):
+        C = run(lvb, torch_cuda, A, Bt, ab, out, c_rowmajor=crm)
+        check(C, A, Bt.T, out)
+
+
+def test_extreme_int8_values_exact(lvb, torch_cuda):
+    # all -128: every product is 16384, K=8192 -> 2^27, exact in int32
+    M, N, K = 256, 256, 8192
+    A = np.full((M, K), -128, dtype=np.int8)
+    Bt = np.full((N, K), -128, dtype=np.int8)
+    C = run(lvb, torch_cuda, A, Bt, "Int8", "Int32")
+    assert np.all(C == 128 * 128 * K)
+
+
+def test_leading_dimensions_and_zero_k(lvb, torch_cuda):
+    torch = torch_cuda
+    A, Bt = gemm_inputs(200, 136, 120, "Float16", seed=9)
+    C = run(lvb, torch, A, Bt, "Float16", "Float32", lda=128, ldb=192, ldc=256)
+    check(C, A, Bt.T, "Float32")
+    C = run(lvb, torch, A, Bt, "Float16", "Float32", c_rowmajor=True, ldc=200)
+    check(C, A, Bt.T, "Float32")
+    # K = 0: C is the empty sum, zero
+    dA = torch.empty(5, 0, dtype=torch.float16, device="cuda")
+    dB = torch.empty(0, 7, dtype=torch.float16, device="cuda")
+    dC = torch.full((5, 7), 3.0, device="cuda")
+    lvb.gemm(dC, dA, dB)
+    torch.cuda.synchronize()
+    assert torch.all(dC == 0)
+
+
+def test_unaligned_rejected_on_device(lvb, torch_cuda):
+    torch = torch_cuda
+    buf = torch.zeros(64 * 64 + 1, dtype=torch.float16, device="cuda")
+    A = buf[1:].view(64, 64)             # 2-byte offset: not 16-byte aligned
+    B = torch.zeros(64, 64, dtype=torch.float16, device="cuda").t()
+    C = torch.zeros(64, 64, device="cuda")
+    with pytest.raises(lvb.LavaError) as e:
+        lvb.gemm(C, A, B)
+    assert e.value.status == lvb.LVB_ERR_UNSUPPORTED
+
+
+def test_deterministic_and_canary(lvb, torch_cuda):
+    torch = torch_cuda
+    A, Bt = gemm_inputs(333, 777, 1000, "Float16", seed=4)
+    dA, dB = to_dev(torch, A, "Float16"), to_dev(torch, Bt, "Float16")
+    # column-major C inside a larger buffer: the rows past M must keep their canary value
+    big = torch.full((777, 400), -5.0, device="cuda")
+    C = big[:, :333].t()
+    lvb.gemm(C, dA, dB.t())
+    first = big.clone()
+    lvb.gemm(C, dA, dB.t())
+    torch.cuda.synchronize()
+    assert torch.equal(first, big)
+    assert torch.all(big[:, 333:] == -5.0)
+
+
+@pytest.mark.slow
+def test_config2_fp16_8192_sampled_rows(lvb, torch_cuda):
+    """C2 at full size: every output row sampled is checked against the float64 oracle."""
+    torch = torch_cuda
+    cfg = GEMM_CONFIGS["C2"]
+    A, Bt = gemm_inputs(cfg["M"], cfg["N"], cfg["K"], cfg["ab"], cfg["seed"])
+    C = run(lvb, torch, A, Bt, "Float16", "Float16")
+    rows = np.random.default_rng(0).choice(cfg["M"], 96, replace=False)
+    rows = np.concatenate([rows, [0, 127, 128, cfg["M"] - 1]])
+    check(C[rows], A[rows], Bt.T, "Float16")
+
+
+@pytest.mark.slow
+def test_config3_int8_8192_exact_sampled_rows(lvb, torch_cuda):
+    torch = torch_cuda
+    cfg = GEMM_CONFIGS["C3"]
+    A, Bt = gemm_inputs(cfg["M"], cfg["N"], cfg["K"], cfg["ab"], cfg["seed"])
+    C = run(lvb, torch, A, Bt, "Int8", "Int32")
+    rows = np.random.default_rng(1).choice(cfg["M"], 96, replace=False)
+    rows = np.concatenate([rows, [0, cfg["M"] - 1]])
+    # float64 BLAS is exact here: every partial sum is an integer below 2^53
+    ref = (A[rows].astype(np.float64) @ Bt.T.astype(np.float64)).astype(np.int64)
+    assert np.array_equal(C[rows].astype(np.int64), ref)
+    # a checksum of every row: sum_n C[m,n] == A[m,:] · (sum_n B[:,n])
+    colsum = Bt.astype(np.int64).sum(axis=0)            # (K,)
+    assert np.array_equal(C.astype(np.int64).sum(axis=1), A.astype(np.int64) @ colsum)
