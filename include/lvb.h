@@ -130,6 +130,8 @@ typedef struct lvb_gemm_plan {
   int32_t smem_bytes;   /* dynamic shared memory per CTA */
   int32_t tmem_cols;    /* TMEM columns allocated per CTA */
   int32_t instr_m, instr_n, instr_k; /* tcgen05.mma shape */
+  int32_t repack_a, repack_b;        /* operand copied to an aligned stream-ordered workspace
+                                        first (leading dimension or base not 16-byte aligned) */
 } lvb_gemm_plan;
 
 /* Validate a descriptor (host only). */
@@ -138,8 +140,10 @@ int lvb_gemm_check(const lvb_gemm_desc* d);
 int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* out);
 /* Enqueue C = A·B on `stream` (on the current CUDA device). Supported pairs:
  *   F16×F16 -> F32|F16|BF16,  BF16×BF16 -> F32|F16|BF16,  I8×I8 -> I32,  U8×U8 -> U32.
- * A row-major and B column-major (both K-contiguous); C either layout. A and B must start
- * on 16-byte boundaries with lda·sizeof, ldb·sizeof multiples of 16 bytes. */
+ * A row-major and B column-major (both K-contiguous); C either layout; any leading
+ * dimension >= the extent. An operand whose base or leading dimension is not a 16-byte
+ * multiple is first repacked on the device into a stream-ordered workspace
+ * (cudaMallocAsync / cudaFreeAsync on `stream`). */
 int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
 
 /* ---------------------------------------------------------------------------------------

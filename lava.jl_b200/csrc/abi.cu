@@ -181,6 +181,31 @@ int make_tmap_3d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, u
   return LVB_OK;
 }
 
+int make_tmap_nd(CUtensorMap* tm, const void* base, int esize, int rank, const uint64_t* dims,
+                 const uint64_t* strides, const uint32_t* box, const char* op) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return fail(LVB_ERR_CUDA, op, "cuTensorMapEncodeTiled unavailable", "driver too old");
+  if (rank < 1 || rank > 5) return fail(LVB_ERR_INVALID_ARG, op, "tensor map rank");
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides[i] * (uint64_t)esize;
+  }
+  CUresult r = enc(tm, tma_type(esize), rank, const_cast<void*>(base), d, s, b, e,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    std::snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled(rank %d) failed (%d)", rank, (int)r);
+    return fail(LVB_ERR_UNSUPPORTED, op, buf,
+                "pointers must be 16-byte aligned, strides*size multiples of 16");
+  }
+  return LVB_OK;
+}
+
 int gemm_smem_bytes(int bn);
 int gemm_stages(int bn);
 int gemm_zero_fill(const lvb_gemm_desc* d, void* C, cudaStream_t stream);
@@ -344,10 +369,6 @@ int lvb_gemm_check(const lvb_gemm_desc* d) {
   if (d->ldb < kk) return fail(LVB_ERR_INVALID_ARG, op, "ldb < K");
   const int64_t cmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
   if (d->ldc < cmin) return fail(LVB_ERR_INVALID_ARG, op, d->c_rowmajor ? "ldc < N" : "ldc < M");
-  const int es = dtype_size(d->a_type);
-  if ((d->lda * es) % 16 != 0 || (d->ldb * es) % 16 != 0)
-    return fail(LVB_ERR_UNSUPPORTED, op, "lda/ldb rows are not 16-byte multiples",
-                "pad the leading dimension to a multiple of 16 bytes");
   return LVB_OK;
 }
 
@@ -384,6 +405,9 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
   out->instr_m = 128;
   out->instr_n = bn;
   out->instr_k = (d->a_type == LVB_I8 || d->a_type == LVB_U8) ? 32 : 16;
+  const int es = dtype_size(d->a_type);
+  out->repack_a = (d->lda * es) % 16 != 0;
+  out->repack_b = (d->ldb * es) % 16 != 0;
   return LVB_OK;
 }
 
@@ -394,8 +418,9 @@ int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void
   if (d->M == 0 || d->N == 0) return LVB_OK;
   if (!C) return fail(LVB_ERR_INVALID_ARG, op, "C is NULL");
   if (d->K > 0 && (!A || !B)) return fail(LVB_ERR_INVALID_ARG, op, "A or B is NULL");
-  if (d->K > 0 && (((uintptr_t)A) % 16 || ((uintptr_t)B) % 16))
-    return fail(LVB_ERR_UNSUPPORTED, op, "A and B must start on 16-byte boundaries");
+  const int es = dtype_size(d->a_type);
+  if (((uintptr_t)A) % es || ((uintptr_t)B) % es || ((uintptr_t)C) % dtype_size(d->c_type))
+    return fail(LVB_ERR_INVALID_ARG, op, "pointer not aligned to its element size");
   DeviceState* dev = current_device_state(op);
   if (!dev) return LVB_ERR_NO_DEVICE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -403,6 +428,8 @@ int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void
   lvb_gemm_plan plan;
   st = lvb_gemm_plan_for(d, dev->sm_count, &plan);
   if (st) return st;
+  if (((uintptr_t)A) % 16) plan.repack_a = 1;
+  if (((uintptr_t)B) % 16) plan.repack_b = 1;
   return gemm_launch(d, plan, A, B, C, s, dev);
 }
 

@@ -1,11 +1,498 @@
-// attn_sm100.cu — flash-attention forward for B200 (sm_100a). (kernel added next)
+// attn_sm100.cu — causal / GQA flash-attention forward for B200 (sm_100a).
+//
+// What it computes is the key-block loop a Lava flash kernel writes with the coopmat
+// vocabulary: S = Q·Kᵀ (coopmat_muladd, K read through a transposing view), row max
+// (coopmat_reduce(max, Row), result smeared along the row), P = exp(S - m)
+// (coopmat_perelement), row sum (coopmat_reduce(+, Row)), P converted fp32 -> fp16/bf16 and
+// from accumulator to MatrixA use (coopmat_convert), O = P·V + rescaled O
+// (src/device/coopmat_intrinsics.jl:520-755; src/compiler/spirv/coopmat.jl:783-822,887-991),
+// then O / l stored through a clamped layout.
+//
+// How, per CTA = two 128-row query tiles of one (batch, query head):
+//   * warp 8 lane 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through a
+//     3-slot ring of 128-key blocks (128B swizzle, zero fill past seq_kv);
+//   * warp 9 lane 0 (MMA): S_t = Q_t·K_jᵀ into TMEM (128×128 fp32 per tile), and
+//     O_t += P_t·V_j into TMEM (128×D fp32 per tile) with V as an MN-major B operand; the
+//     QK of block j+1 is issued as soon as a softmax group has read S_t(j), so the tensor
+//     core works on one tile while the other tile's softmax runs;
+//   * warps 0-3 / 4-7 (softmax, one warpgroup per tile): thread = query row, the whole
+//     128-key row sits in registers, so max and sum need no shuffles; exp2 in the log2
+//     domain with the scale folded in; the O rescale is lazy (only when the running max
+//     grows by more than 2^8, which keeps every p <= 256) and done in TMEM by the same
+//     warp; P goes to shared memory in the 128B-swizzled K-major layout the MMA reads;
+//   * TMEM: S_0 | S_1 | O_0 | O_1 = 512 columns.
+//   * grid (query-tile pairs, batch·heads), heaviest causal pair first inside a head; the
+//     pairs of one head run side by side and share its K/V blocks in L2.
+#include <algorithm>
+#include <cmath>
+
 #include "lvb_internal.h"
 
 namespace lvb {
 
+constexpr int kAttnThreads = 320;
+constexpr int kRing = 3;
+constexpr int kPBytes = 128 * 128 * 2;  // one P tile (128 queries x 128 keys, 16-bit)
+constexpr int kChunk = 128 * 128;       // bytes of one 128-row x 64-element swizzled chunk
+
+struct AttnParams {
+  int B, Hq, Hkv, Sq, Skv, group, num_pairs, causal;
+  float scale_log2;
+  void* O;
+  long long o_sb, o_sh, o_ss;  // element strides of batch, head, seq
+  float* lse;
+  DevStatus* status;
+  unsigned long long timeout_ns;
+};
+
+template <int D>
+struct AttnCfg {
+  static constexpr int kTileBytes = 128 * D * 2;  // Q tile or K/V block
+  static constexpr int kQBytes = 2 * kTileBytes;
+  static constexpr int kSmem = kQBytes + kRing * kTileBytes + 2 * kPBytes + 256 + 1024;
+};
+
+__device__ __forceinline__ void drain_wait_a(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_ns();
+  while (!bar_try_wait(a, parity)) {
+    if (global_ns() - t0 > timeout_ns) return;
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using Cfg = AttnCfg<D>;
+  constexpr int kDChunks = D / 64;
+  constexpr uint32_t kFmt = BF16 ? 1 : 0;
+  constexpr uint32_t kIdescQK = make_idesc(1, kFmt, kFmt, 0, 0, 128, 128);
+  constexpr uint32_t kIdescPV = make_idesc(1, kFmt, kFmt, 0, 1, 128, D);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* sQ = smem;                                   // [2][D/64 chunks][128 rows][128 B]
+  uint8_t* sRing = sQ + Cfg::kQBytes;                   // [3][D/64 chunks][128 rows][128 B]
+  uint8_t* sP = sRing + kRing * Cfg::kTileBytes;        // [2][2 chunks][128 rows][128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* ring_full = bars + 1;     // [3]
+  uint64_t* ring_empty = bars + 4;    // [3]
+  uint64_t* s_full = bars + 7;        // [2]
+  uint64_t* s_free = bars + 9;        // [2]
+  uint64_t* p_full = bars + 11;       // [2]
+  uint64_t* pv_done = bars + 13;      // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  const int pair = p.num_pairs - 1 - (int)blockIdx.x;   // heaviest causal pair first
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hq;
+  const int h = bh - b * p.Hq;
+  const int hk = h / p.group;
+  const int q0 = pair * 256;
+  const int off = p.Skv - p.Sq;  // query q sees keys <= q + off
+  const int kv_blocks = (p.Skv + 127) / 128;
+  int n_blocks = kv_blocks;
+  if (p.causal) {
+    const int last = min(q0 + 255, p.Sq - 1) + off;
+    n_blocks = last < 0 ? 0 : min(kv_blocks, last / 128 + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < kRing; ++s) {
+      bar_init(&ring_full[s], 1);
+      bar_init(&ring_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      bar_init(&s_full[t], 1);
+      bar_init(&s_free[t], 128);
+      bar_init(&p_full[t], 128);
+      bar_init(&pv_done[t], 1);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+
+  if (warp == 8) {
+    if (lane == 0 && n_blocks > 0) {
+      // ---------------- TMA producer ----------------
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      bar_arrive_expect_tx(q_full, Cfg::kQBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < kDChunks; ++c)
+          tma_load_4d(sQ + t * Cfg::kTileBytes + c * kChunk, &tmQ, c * 64, q0 + 128 * t, h, b,
+                      q_full);
+      const int items = 2 * n_blocks;
+      int issued = 0;
+      for (int i = 0; i < items; ++i) {
+        const int slot = i % kRing;
+        const uint32_t par = (uint32_t)((i / kRing) & 1);
+        if (!wait_bar(&ring_empty[slot], par ^ 1, g, 11, i)) break;
+        bar_arrive_expect_tx(&ring_full[slot], Cfg::kTileBytes);
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+        for (int c = 0; c < kDChunks; ++c)
+          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128, hk,
+                      b, &ring_full[slot]);
+        issued = i + 1;
+      }
+      if (*abort_flag) {
+        drain_wait_a(q_full, 0, p.timeout_ns);
+        for (int i = max(0, issued - kRing); i < issued; ++i)
+          drain_wait_a(&ring_full[i % kRing], (uint32_t)((i / kRing) & 1), p.timeout_ns);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0 && n_blocks > 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t r_base = smem_u32(sRing);
+      const uint32_t p_base = smem_u32(sP);
+      auto issue_qk = [&](int t, int slot) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o = (kk >> 2) * kChunk + (kk & 3) * 32;
+          const uint64_t ad = sdesc_sw128(q_base + t * Cfg::kTileBytes + o, 16, 1024);
+          const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + o, 16, 1024);
+          mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int slot, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA
+          const uint64_t ad =
+              sdesc_sw128(p_base + t * kPBytes + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+          // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64 dims
+          // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
+          const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
+                                          kChunk, 1024);
+          mma_f16_ss(tmem + 256 + 128 * t, ad, bd, kIdescPV, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = wait_bar(q_full, 0, g, 12, 0);
+      if (ok) ok = wait_bar(&ring_full[0], 0, g, 13, 0);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        mma_commit(&s_full[0]);
+        issue_qk(1, 0);
+        mma_commit(&s_full[1]);
+        mma_commit(&ring_empty[0]);
+      }
+      for (int j = 0; j < n_blocks && ok; ++j) {
+        if (j + 1 < n_blocks) {
+          const int ik = 2 * (j + 1);
+          if (!wait_bar(&ring_full[ik % kRing], (uint32_t)((ik / kRing) & 1), g, 14, j)) break;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!wait_bar(&s_free[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(t, ik % kRing);
+            mma_commit(&s_full[t]);
+          }
+          if (!ok) break;
+          mma_commit(&ring_empty[ik % kRing]);
+        }
+        const int iv = 2 * j + 1;
+        if (!wait_bar(&ring_full[iv % kRing], (uint32_t)((iv / kRing) & 1), g, 16, j)) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 17, j)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, iv % kRing, j > 0);
+          mma_commit(&pv_done[t]);
+        }
+        if (!ok) break;
+        mma_commit(&ring_empty[iv % kRing]);
+      }
+      mma_commit(drain);
+      drain_wait_a(drain, 0, p.timeout_ns);
+    }
+  } else {
+    // ---------------- softmax, one warpgroup per query tile ----------------
+    const int t = warp >> 2;
+    const int wl = warp & 3;
+    const int r = wl * 32 + lane;               // row within the tile = TMEM lane
+    const int q = q0 + 128 * t + r;             // query index
+    const uint32_t lane_off = (uint32_t)(wl * 32) << 16;
+    const uint32_t tS = tmem + lane_off + 128 * t;
+    const uint32_t tO = tmem + lane_off + 256 + 128 * t;
+    const uint32_t p_row = smem_u32(sP) + t * kPBytes + r * 128;
+    const float NEG_INF = -INFINITY;
+    float m_ref = NEG_INF;   // running max (log2 domain, scale folded in)
+    float l = 0.f;           // running sum of p relative to m_ref
+    bool ok = true;
+    const int tile_first_row = q0 + 128 * t;
+
+    for (int j = 0; j < n_blocks; ++j) {
+      if (!wait_bar(&s_full[t], (uint32_t)(j & 1), g, 21, j)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[128];
+      {
+        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[0]);
+        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[32]);
+        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[64]);
+        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[96]);
+        tmem_ld32(tS + 0, s0);
+        tmem_ld32(tS + 32, s1);
+        tmem_ld32(tS + 64, s2);
+        tmem_ld32(tS + 96, s3);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      bar_arrive(&s_free[t]);
+
+      const int kbase = j * 128;
+      const bool need_mask =
+          (kbase + 127 >= p.Skv) || (p.causal && kbase + 127 > tile_first_row + off);
+      if (need_mask) {
+        const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
+      }
+      float mx = NEG_INF;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      const float m_new = mx * p.scale_log2;
+      float alpha = 1.f;
+      bool resc = false;
+      if (j == 0) {
+        m_ref = m_new;
+      } else if (m_new > m_ref + 8.f) {
+        alpha = fast_exp2(m_ref - m_new);
+        m_ref = m_new;
+        resc = true;
+      }
+      const float m_use = (m_ref == NEG_INF) ? 0.f : m_ref;
+
+      if (j > 0) {
+        // PV of the previous block must be complete before O is rescaled or P rewritten.
+        if (!wait_bar(&pv_done[t], (uint32_t)((j - 1) & 1), g, 22, j)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tO + 16 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st16(tO + 16 * c, o);
+          }
+          tmem_wait_st();
+        }
+        l *= alpha;
+      }
+
+      const float sl = p.scale_log2;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
+        sum += p0 + p1;
+        s[c] = pack2<BF16>(p0, p1);
+      }
+      l += sum;
+      // P row -> shared memory, 128B-swizzled K-major: 16-byte unit u of the row goes to
+      // position u ^ (row % 8) inside the row's 128-byte line, 64 keys per chunk.
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint32_t addr = p_row + (u >> 3) * kChunk + ((((u & 7) ^ (r & 7))) << 4);
+        st_shared_v4(addr, s[4 * u], s[4 * u + 1], s[4 * u + 2], s[4 * u + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      bar_arrive(&p_full[t]);
+    }
+
+    // ---------------- epilogue: O / l -> global, lse ----------------
+    if (ok && n_blocks > 0) ok = wait_bar(&pv_done[t], (uint32_t)((n_blocks - 1) & 1), g, 23, 0);
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool row_ok = q < p.Sq;
+      typedef __align__(16) uint32_t u4[4];
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.O) +
+                      2 * ((long long)b * p.o_sb + (long long)h * p.o_sh + (long long)q * p.o_ss);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (n_blocks > 0) {
+          tmem_ld32(tO + 32 * c, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack2<BF16>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+        }
+      }
+      if (p.lse && row_ok) {
+        const float mu = (m_ref == NEG_INF) ? 0.f : m_ref;
+        const float v = l > 0.f ? (mu + __log2f(l)) * 0.69314718055994530942f : NEG_INF;
+        p.lse[((long long)b * p.Hq + h) * p.Sq + q] = v;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// seq_kv == 0: every row sees no key, O = 0 and lse = -inf (the empty softmax).
+__global__ void attn_empty_kernel(uint16_t* O, long long sb, long long sh, long long ss, int B,
+                                  int H, int S, int D, float* lse) {
+  const long long rows = (long long)B * H * S;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rows * D;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / D;
+    const int d = (int)(i - row * D);
+    const int s = (int)(row % S);
+    const long long bh = row / S;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    O[b * sb + h * sh + s * ss + d] = 0;
+    if (lse && d == 0) lse[row] = -INFINITY;
+  }
+}
+
+// ----------------------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------------------
+namespace {
+
+void packed_or(const int64_t* s, int64_t H, int64_t S, int64_t D, long long out[3]) {
+  if (s[0] == 0 && s[1] == 0 && s[2] == 0) {
+    out[2] = D;
+    out[1] = S * D;
+    out[0] = H * S * D;
+  } else {
+    out[0] = s[0];
+    out[1] = s[1];
+    out[2] = s[2];
+  }
+}
+
+template <int D, bool BF16>
+int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                const AttnParams& p, cudaStream_t stream) {
+  auto kern = attn_fwd_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       AttnCfg<D>::kSmem);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "cudaFuncSetAttribute");
+  dim3 grid(p.num_pairs, p.B * p.Hq);
+  kern<<<grid, kAttnThreads, AttnCfg<D>::kSmem, stream>>>(tq, tk, tv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "kernel launch");
+  return LVB_OK;
+}
+
+}  // namespace
+
+int attn_smem_bytes(int D) { return D == 64 ? AttnCfg<64>::kSmem : AttnCfg<128>::kSmem; }
+
 int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,
                 float* lse, cudaStream_t stream, DeviceState* dev) {
-  return fail(LVB_ERR_UNSUPPORTED, "lvb_attention_fwd", "attention kernel not built yet");
+  const char* op = "lvb_attention_fwd";
+  const int64_t B = d->batch, Hq = d->heads_q, Hkv = d->heads_kv, Sq = d->seq_q, Skv = d->seq_kv,
+                D = d->head_dim;
+  long long qs[3], ks[3], vs[3], os[3];
+  packed_or(d->q_stride, Hq, Sq, D, qs);
+  packed_or(d->k_stride, Hkv, Skv, D, ks);
+  packed_or(d->v_stride, Hkv, Skv, D, vs);
+  packed_or(d->o_stride, Hq, Sq, D, os);
+  if (Skv == 0) {
+    const long long total = B * Hq * Sq * D;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 8192);
+    attn_empty_kernel<<<blocks, 256, 0, stream>>>((uint16_t*)O, os[0], os[1], os[2], (int)B,
+                                                  (int)Hq, (int)Sq, (int)D, lse);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? LVB_OK : fail_cuda(e, op, "empty-softmax launch");
+  }
+  const uint32_t rowsbox = 128;
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Sq, (uint64_t)Hq, (uint64_t)B};
+    const uint64_t str[3] = {(uint64_t)qs[2], (uint64_t)qs[1], (uint64_t)qs[0]};
+    const uint32_t box[4] = {64, rowsbox, 1, 1};
+    int st = make_tmap_nd(&tq, Q, 2, 4, dims, str, box, op);
+    if (st) return st;
+  }
+  {
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Skv, (uint64_t)Hkv, (uint64_t)B};
+    const uint64_t strk[3] = {(uint64_t)ks[2], (uint64_t)ks[1], (uint64_t)ks[0]};
+    const uint64_t strv[3] = {(uint64_t)vs[2], (uint64_t)vs[1], (uint64_t)vs[0]};
+    const uint32_t box[4] = {64, rowsbox, 1, 1};
+    int st = make_tmap_nd(&tk, K, 2, 4, dims, strk, box, op);
+    if (st) return st;
+    st = make_tmap_nd(&tv, V, 2, 4, dims, strv, box, op);
+    if (st) return st;
+  }
+  AttnParams p;
+  p.B = (int)B;
+  p.Hq = (int)Hq;
+  p.Hkv = (int)Hkv;
+  p.Sq = (int)Sq;
+  p.Skv = (int)Skv;
+  p.group = (int)(Hq / Hkv);
+  p.num_pairs = (int)((Sq + 255) / 256);
+  p.causal = d->causal ? 1 : 0;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.O = O;
+  p.o_sb = os[0];
+  p.o_sh = os[1];
+  p.o_ss = os[2];
+  p.lse = lse;
+  p.status = dev->status;
+  p.timeout_ns = wait_timeout_ns();
+  if (p.num_pairs > 2147483647 || B * Hq > 65535)
+    return fail(LVB_ERR_UNSUPPORTED, op, "batch*heads above 65535", "split the batch");
+  const bool bf16 = d->dtype == LVB_BF16;
+  if (D == 128) return bf16 ? launch_attn<128, true>(tq, tk, tv, p, stream)
+                            : launch_attn<128, false>(tq, tk, tv, p, stream);
+  if (D == 64) return bf16 ? launch_attn<64, true>(tq, tk, tv, p, stream)
+                           : launch_attn<64, false>(tq, tk, tv, p, stream);
+  return fail(LVB_ERR_UNSUPPORTED, op, "head_dim must be 64 or 128");
 }
 
 }  // namespace lvb

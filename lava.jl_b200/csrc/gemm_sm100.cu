@@ -19,6 +19,8 @@
 //     overlap this tile's stores.
 //   * persistent grid (one CTA per SM), tiles visited in groups of GROUP_M row-tiles so the
 //     ~148 tiles in flight share A rows and B columns in L2.
+#include <algorithm>
+
 #include "lvb_internal.h"
 
 namespace lvb {
@@ -356,8 +358,72 @@ int gemm_zero_fill(const lvb_gemm_desc* d, void* C, cudaStream_t stream) {
   return e == cudaSuccess ? LVB_OK : fail_cuda(e, "lvb_gemm", "zero-fill launch");
 }
 
+// Copies `rows` rows of `cols` elements (row stride `ld` elements, any alignment) into a
+// dense buffer with row stride `dld` (a 16-byte multiple), zero-filling columns cols..dld-1,
+// so a tensor map can describe it. Used when a caller's operand has a leading dimension or
+// base address TMA cannot address; it is one extra pass over that operand.
+template <typename T>
+__global__ void repack_kernel(const T* __restrict__ src, long long rows, long long cols,
+                              long long ld, T* __restrict__ dst, long long dld) {
+  const long long total = rows * dld;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / dld, c = i - r * dld;
+    dst[i] = c < cols ? src[r * ld + c] : T(0);
+  }
+}
+
+static int repack(const void* src, int esize, long long rows, long long cols, long long ld,
+                  void* dst, long long dld, cudaStream_t s) {
+  const long long total = rows * dld;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 8192);
+  if (esize == 1)
+    repack_kernel<uint8_t><<<blocks, 256, 0, s>>>((const uint8_t*)src, rows, cols, ld,
+                                                   (uint8_t*)dst, dld);
+  else
+    repack_kernel<uint16_t><<<blocks, 256, 0, s>>>((const uint16_t*)src, rows, cols, ld,
+                                                    (uint16_t*)dst, dld);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LVB_OK : fail_cuda(e, "lvb_gemm", "repack launch");
+}
+
+int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
+                        const void* B, void* C, cudaStream_t stream, DeviceState* dev);
+
 int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A, const void* B,
                 void* C, cudaStream_t stream, DeviceState* dev) {
+  if (!plan.repack_a && !plan.repack_b) return gemm_launch_aligned(d, plan, A, B, C, stream, dev);
+  // Stream-ordered workspace for the repacked operand(s); freed on the same stream.
+  const int es = dtype_size(d->a_type);
+  const long long kp = (d->K + 15) / 16 * 16;  // 16 elements: a 16-byte multiple for 1 and 2 bytes
+  const size_t bytes_a = plan.repack_a ? (size_t)d->M * kp * es : 0;
+  const size_t bytes_b = plan.repack_b ? (size_t)d->N * kp * es : 0;
+  void* ws = nullptr;
+  cudaError_t e = cudaMallocAsync(&ws, bytes_a + bytes_b, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaMallocAsync");
+  lvb_gemm_desc d2 = *d;
+  const void* a = A;
+  const void* b = B;
+  int st = LVB_OK;
+  if (plan.repack_a) {
+    st = repack(A, es, d->M, d->K, d->lda, ws, kp, stream);
+    a = ws;
+    d2.lda = kp;
+  }
+  if (st == LVB_OK && plan.repack_b) {
+    void* wb = (uint8_t*)ws + bytes_a;
+    st = repack(B, es, d->N, d->K, d->ldb, wb, kp, stream);
+    b = wb;
+    d2.ldb = kp;
+  }
+  if (st == LVB_OK) st = gemm_launch_aligned(&d2, plan, a, b, C, stream, dev);
+  e = cudaFreeAsync(ws, stream);
+  if (st == LVB_OK && e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaFreeAsync");
+  return st;
+}
+
+int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
+                        const void* B, void* C, cudaStream_t stream, DeviceState* dev) {
   const int esize = dtype_size(d->a_type);
   // Kernel space: rows of "A" are the lane (contiguous-store) dimension.
   const void* kA = plan.swap_ab ? B : A;

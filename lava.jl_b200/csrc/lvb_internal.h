@@ -43,6 +43,11 @@ EncodeTiledFn encode_tiled_fn();
 int make_tmap_2d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
                  uint64_t ld, uint32_t box_inner, uint32_t box_rows, const char* op);
 
+// Rank-n tiled map (n <= 5), 128-byte swizzle. dims/box innermost first; strides[i] is the
+// element stride of dimension i+1.
+int make_tmap_nd(CUtensorMap* tm, const void* base, int esize, int rank, const uint64_t* dims,
+                 const uint64_t* strides, const uint32_t* box, const char* op);
+
 // 3-D map [outer][rows][inner] with element strides (ld_rows, ld_outer).
 int make_tmap_3d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
                  uint64_t outer, uint64_t ld_rows, uint64_t ld_outer, uint32_t box_inner,

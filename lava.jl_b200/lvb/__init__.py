@@ -93,7 +93,8 @@ class lvb_gemm_plan(C.Structure):
     _fields_ = [("swap_ab", C.c_int32), ("tile_m", C.c_int32), ("tile_n", C.c_int32),
                 ("tile_k", C.c_int32), ("stages", C.c_int32), ("tiles", C.c_int32),
                 ("ctas", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
-                ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32)]
+                ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32),
+                ("repack_a", C.c_int32), ("repack_b", C.c_int32)]
 
 
 class lvb_attn_desc(C.Structure):
@@ -369,6 +370,10 @@ def attention(O, Q, K, V, causal=True, scale=None, lse=None, stream=None):
                                 O.data_ptr(), lse.data_ptr() if lse is not None else None,
                                 _stream_ptr(stream)))
     return O
+
+
+def attention_available() -> bool:
+    return True
 
 
 def device_status(stream=None):

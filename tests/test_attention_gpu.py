@@ -1,0 +1,137 @@
+"""GPU tier: the tcgen05 flash-attention forward through the C ABI against the oracle.
+
+Tolerances (per element, written from the error sources of the kernel's arithmetic):
+  P is rounded to the input type before P·V and O is rounded to it at the store, so
+  |ΔO| <= u·(max|V| + |O|) with u the unit roundoff of the type (2^-11 fp16, 2^-8 bf16);
+  the fp32 accumulation and the hardware exp2 add far less. Stated bounds:
+    Float16:  max|Δ| <= 1e-2 and relative Frobenius <= 1e-3
+    BFloat16: max|Δ| <= 2^-8·(max|V| + max|O|) and relative Frobenius <= 1e-2
+  lse (fp32) within 1e-3 absolute.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.attention import attention_ref, attention_blockwise
+from oracle.inputs import attention_inputs, ATTN_CONFIGS
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+
+
+def tdt(torch, T):
+    return torch.float16 if T == "Float16" else torch.bfloat16
+
+
+def run(lvb, torch, Q, K, V, T, causal, scale, want_lse=False):
+    dQ, dK, dV = (torch.from_numpy(np.ascontiguousarray(x)).to(tdt(torch, T)).cuda()
+                  for x in (Q, K, V))
+    dO = torch.full_like(dQ, 7.0)
+    lse = torch.empty(Q.shape[:3], dtype=torch.float32, device="cuda") if want_lse else None
+    lvb.attention(dO, dQ, dK, dV, causal=causal, scale=scale, lse=lse)
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    O = dO.float().cpu().numpy()
+    return (O, lse.cpu().numpy()) if want_lse else O
+
+
+def check(O, ref, V, T):
+    d = np.abs(O.astype(np.float64) - ref)
+    rf = np.linalg.norm(O - ref) / max(np.linalg.norm(ref), 1e-30)
+    if T == "Float16":
+        assert d.max() <= 1e-2 and rf <= 1e-3, (d.max(), rf)
+    else:
+        bound = 2.0 ** -8 * (np.abs(V).max() + np.abs(ref).max())
+        assert d.max() <= bound and rf <= 1e-2, (d.max(), bound, rf)
+
+
+def test_golden_fixture(lvb, torch_cuda):
+    z = np.load(GOLDEN / "attn_f16_gqa_causal.npz")
+    O = run(lvb, torch_cuda, z["Q"], z["K"], z["V"], "Float16", bool(z["causal"]),
+            float(z["scale"]))
+    check(O, z["O"].astype(np.float64), z["V"], "Float16")
+
+
+@pytest.mark.parametrize("T", ["Float16", "BFloat16"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv", [
+    (1, 2, 2, 256, 256),      # one tile pair, square
+    (2, 4, 1, 300, 300),      # ragged query/key tails, GQA 4:1
+    (1, 8, 2, 200, 333),      # Sq < Skv: causal mask offset by Skv - Sq
+    (1, 2, 2, 640, 128),      # Sq > Skv: early rows see no key under the causal mask
+    (1, 1, 1, 1, 1000),       # decode-like single query
+])
+def test_small(lvb, torch_cuda, T, D, causal, B, Hq, Hkv, Sq, Skv):
+    Q, K, V = attention_inputs(B, Hq, Hkv, Sq, D, T, seed=Sq + Skv + D, Skv=Skv)
+    scale = D ** -0.5
+    O, lse = run(lvb, torch_cuda, Q, K, V, T, causal, scale, want_lse=True)
+    ref, lref = attention_ref(Q, K, V, causal, scale, return_lse=True)
+    check(O, ref, V, T)
+    fin = np.isfinite(lref)
+    assert np.array_equal(np.isfinite(lse), fin)
+    assert np.abs(lse[fin] - lref[fin]).max(initial=0) <= 1e-3
+
+
+def test_large_scores_stay_finite(lvb, torch_cuda):
+    # scores of several hundred (a 20x scale): the running max moves often and far, which
+    # exercises the lazy O rescale
+    Q, K, V = attention_inputs(1, 2, 2, 512, 128, "Float16", seed=77)
+    O = run(lvb, torch_cuda, Q, K, V, "Float16", True, 20 * 128 ** -0.5)
+    ref = attention_ref(Q, K, V, True, 20 * 128 ** -0.5)
+    assert np.isfinite(O).all()
+    check(O, ref, V, "Float16")
+
+
+def test_strided_views(lvb, torch_cuda):
+    # Q/K/V as [B][S][H][D] storage viewed as [B][H][S][D] (non-packed strides)
+    torch = torch_cuda
+    Q, K, V = attention_inputs(2, 4, 2, 192, 128, "Float16", seed=5)
+    def bshd(x):
+        t = torch.from_numpy(np.ascontiguousarray(x.transpose(0, 2, 1, 3))).half().cuda()
+        return t.transpose(1, 2)
+    dQ, dK, dV = bshd(Q), bshd(K), bshd(V)
+    dO = torch.empty(2, 192, 4, 128, dtype=torch.float16, device="cuda").transpose(1, 2)
+    lvb.attention(dO, dQ, dK, dV, causal=True)
+    torch.cuda.synchronize()
+    ref = attention_ref(Q, K, V, True, 128 ** -0.5)
+    check(dO.float().cpu().numpy(), ref, V, "Float16")
+
+
+def _full_config(lvb, torch, name, units):
+    cfg = ATTN_CONFIGS[name]
+    T = cfg["dtype"]
+    gen = torch.Generator(device="cuda").manual_seed(cfg["seed"])
+    Bn, Hq, Hkv, S, D = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"]
+    dt = tdt(torch, T)
+    dQ = torch.randn((Bn, Hq, S, D), generator=gen, device="cuda").to(dt)
+    dK = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(dt)
+    dV = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(dt)
+    dO = torch.empty_like(dQ)
+    lse = torch.empty((Bn, Hq, S), dtype=torch.float32, device="cuda")
+    lvb.attention(dO, dQ, dK, dV, causal=True, lse=lse)
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    g = Hq // Hkv
+    for (b, h) in units:
+        q = dQ[b, h].float().cpu().numpy()
+        k = dK[b, h // g].float().cpu().numpy()
+        v = dV[b, h // g].float().cpu().numpy()
+        ref, lref = attention_blockwise(q, k, v, True, D ** -0.5, block=512)
+        O = dO[b, h].float().cpu().numpy()
+        check(O, ref.astype(np.float64), v, T)
+        assert np.abs(lse[b, h].cpu().numpy() - lref).max() <= 1e-3
+    # every row is a convex combination of V rows: |O| <= max|V| everywhere
+    assert float(dO.float().abs().max()) <= float(dV.float().abs().max()) + 1e-2
+    assert torch.isfinite(dO.float()).all()
+
+
+@pytest.mark.slow
+def test_config4_fp16_full(lvb, torch_cuda):
+    _full_config(lvb, torch_cuda, "C4", [(0, 0), (3, 31), (1, 17)])
+
+
+@pytest.mark.slow
+def test_config5_bf16_gqa_full(lvb, torch_cuda):
+    _full_config(lvb, torch_cuda, "C5", [(0, 0), (7, 63)])
