@@ -1,0 +1,73 @@
+# LavaB200 tests. Tier 1 (no GPU): the library loads, caps/shape answers, argument errors.
+# Tier 2 (GPU, when a B200 is visible): gemm!/attention! against a host reference.
+using Test
+using LavaB200
+using LinearAlgebra
+
+@testset "LavaB200" begin
+    @testset "caps (no GPU)" begin
+        c = caps_raw()
+        @test c.coopmat && c.tile == 16 && c.subgroup == 32 && c.cores == 148
+        shapes = matrix_shapes_raw()
+        @test any(s -> s.M == 16 && s.N == 16 && s.K == 16 && s.ab == LavaB200.F16 &&
+                       s.acc == LavaB200.F32, shapes)
+    end
+
+    @testset "argument errors surface as LavaB200Error" begin
+        d = LavaB200.GemmDesc(LavaB200.F16, LavaB200.F16, LavaB200.I32, 1, 0, 0, 64, 64, 64,
+                              64, 64, 64)
+        st = ccall(LavaB200.sym(:lvb_gemm_check), Cint, (Ref{LavaB200.GemmDesc},), d)
+        @test st == LavaB200.LVB_ERR_UNSUPPORTED
+        err = try
+            LavaB200.check(st)
+        catch e
+            e
+        end
+        @test err isa LavaB200Error && err.operation == "lvb_gemm"
+    end
+
+    if LavaB200.device_count() > 0
+        @testset "gemm! Float16 -> Float32 (GPU)" begin
+            M, N, K = 300, 200, 136
+            A = Float16.(rand(Float32, K, M) .* 2 .- 1)    # storage of row-major A (M×K)
+            B = Float16.(rand(Float32, K, N) .* 2 .- 1)    # column-major B (K×N)
+            dA, dB = B200Array(A), B200Array(B)
+            dC = B200Array{Float32}(undef, M, N)
+            gemm!(dC, transpose(dA), dB)
+            C = Array(dC)
+            ref = Float64.(transpose(A)) * Float64.(B)
+            @test maximum(abs.(C .- ref)) <= 1e-2
+            @test device_status() == (0, 0, 0)
+        end
+        @testset "gemm! Int8 exact (GPU)" begin
+            M, N, K = 130, 70, 256
+            A = rand(Int8, K, M); B = rand(Int8, K, N)
+            dC = B200Array{Int32}(undef, M, N)
+            gemm!(dC, transpose(B200Array(A)), B200Array(B))
+            @test Array(dC) == Int32.(transpose(Int64.(A)) * Int64.(B))
+        end
+        @testset "attention! causal GQA (GPU)" begin
+            E, L, Hq, Hkv, Bt = 128, 256, 4, 2, 1
+            Q = Float16.(randn(Float32, E, L, Hq, Bt))
+            K = Float16.(randn(Float32, E, L, Hkv, Bt))
+            V = Float16.(randn(Float32, E, L, Hkv, Bt))
+            dO = B200Array{Float16}(undef, E, L, Hq, Bt)
+            attention!(dO, B200Array(Q), B200Array(K), B200Array(V); causal = true)
+            O = Float64.(Array(dO))
+            g = Hq ÷ Hkv
+            for h in 1:Hq
+                q = Float64.(Q[:, :, h, 1]); k = Float64.(K[:, :, (h - 1) ÷ g + 1, 1])
+                v = Float64.(V[:, :, (h - 1) ÷ g + 1, 1])
+                s = (k' * q) ./ sqrt(E)                       # (Lk, Lq)
+                for i in 1:L, j in 1:L
+                    j > i && (s[j, i] = -Inf)
+                end
+                p = exp.(s .- maximum(s; dims = 1))
+                ref = v * (p ./ sum(p; dims = 1))
+                @test maximum(abs.(O[:, :, h, 1] .- ref)) <= 1e-2
+            end
+        end
+    else
+        @info "no GPU visible: GPU tier not run"
+    end
+end

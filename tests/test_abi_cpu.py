@@ -31,6 +31,30 @@ def test_exports_every_declared_symbol(lvb):
         assert hasattr(lvb.lib, s)
 
 
+def test_struct_layouts_match_header(lvb, tmp_path):
+    """The ctypes mirrors (and so the Julia structs written field for field like them) have
+    the C structs' sizes and field offsets, compiled from include/lvb.h by the host gcc."""
+    structs = {"lvb_matrix_shape": lvb.lvb_matrix_shape, "lvb_device_caps": lvb.lvb_device_caps,
+               "lvb_gemm_desc": lvb.lvb_gemm_desc, "lvb_gemm_plan": lvb.lvb_gemm_plan,
+               "lvb_attn_desc": lvb.lvb_attn_desc}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "lvb.h"', "int main(void){"]
+    for name, cls in structs.items():
+        lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
+        for f, _ in cls._fields_:
+            lines.append(f'printf("{name}.{f} %zu\\n", offsetof({name}, {f}));')
+    lines.append("return 0;}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    out = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True,
+                                                         text=True, check=True).stdout.split("\n") if l)
+    for name, cls in structs.items():
+        assert int(out[name]) == C.sizeof(cls), name
+        for f, _ in cls._fields_:
+            assert int(out[f"{name}.{f}"]) == getattr(cls, f).offset, f"{name}.{f}"
+
+
 def test_library_needs_no_libcuda_at_load(lvb):
     out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
     assert "libcuda.so" not in out

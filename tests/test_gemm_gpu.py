@@ -87,8 +87,11 @@ def check(C, A, B, out):
     A64, B64 = A.astype(np.float64), B.astype(np.float64)
     exact = A64 @ B64
     C64 = np.asarray(C, dtype=np.float64)
-    assert rel_frobenius(C64, exact) <= 1e-3
+    # against the oracle rounded once to the output type (a bf16 output rounded exactly
+    # already sits ~1.7e-3 from the exact product, so the exact product is no yardstick there)
+    assert rel_frobenius(C64, ref) <= 1e-3
     if out == "Float32":
+        assert rel_frobenius(C64, exact) <= 1e-3
         assert max_abs(C64, exact) <= 1e-2
     # per element: one unit of the output type plus the fp32 accumulation bound
     K = A.shape[1]
