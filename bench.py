@@ -374,21 +374,23 @@ def run_gpu(args, w):
     value = units * world / (ms * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers ----
-    h_ins = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
-    h_outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+    h_ins = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins] if not args.no_e2e else []
+    h_outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs] if not args.no_e2e else []
     for h, t in zip(h_ins, ins):
         h.copy_(t)
-    e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(2):
-        step_e2e(h_ins, h_outs)
-    barrier()
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        step_e2e(h_ins, h_outs)
-    e1.record(stream)
-    e1.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    barrier()
+    e2e_steps = 0 if args.no_e2e else max(3, min(args.steps, 20))
+    e2e_ms = float("nan")
+    if e2e_steps:
+        for _ in range(2):
+            step_e2e(h_ins, h_outs)
+        barrier()
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            step_e2e(h_ins, h_outs)
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+        barrier()
     h2d = sum(t.numel() * t.element_size() for t in ins)
     d2h = sum(t.numel() * t.element_size() for t in outs)
 
@@ -417,7 +419,7 @@ def run_gpu(args, w):
                          "frac": achieved / peak, "traffic": traffic,
                          "peak_source": f"{src} burst bf16_tflops (MEASURED_PEAKS.json)"
                          if src.startswith("measured") else f"{src} 1.59 PFLOP/s"},
-            "e2e": {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
+            "e2e": None if args.no_e2e else {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps,
                     "path": "lvb Python binding -> liblvb C ABI; pinned host buffers; "
@@ -440,6 +442,8 @@ def main():
     ap.add_argument("--workload", default="gemm_f16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="lvb", choices=["lvb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the end-to-end leg (used for short profiling runs)")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.steps is None:

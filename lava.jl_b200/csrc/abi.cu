@@ -361,12 +361,12 @@ int lvb_gemm_check(const lvb_gemm_desc* d) {
     return fail(LVB_ERR_UNSUPPORTED, op, m,
                 "supported: Float16/BFloat16 -> Float32/Float16/BFloat16, Int8 -> Int32, UInt8 -> UInt32");
   }
-  if (d->a_rowmajor != 1 || d->b_rowmajor != 0)
+  // An empty operand (K == 0) has no layout to check: C is the empty sum.
+  if (d->K > 0 && (d->a_rowmajor != 1 || d->b_rowmajor != 0))
     return fail(LVB_ERR_UNSUPPORTED, op, "A must be row-major and B column-major (K contiguous)",
                 "pass the transposed product or transpose the operand");
-  const int64_t kk = std::max<int64_t>(1, d->K);
-  if (d->lda < kk) return fail(LVB_ERR_INVALID_ARG, op, "lda < K");
-  if (d->ldb < kk) return fail(LVB_ERR_INVALID_ARG, op, "ldb < K");
+  if (d->K > 0 && d->lda < d->K) return fail(LVB_ERR_INVALID_ARG, op, "lda < K");
+  if (d->K > 0 && d->ldb < d->K) return fail(LVB_ERR_INVALID_ARG, op, "ldb < K");
   const int64_t cmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
   if (d->ldc < cmin) return fail(LVB_ERR_INVALID_ARG, op, d->c_rowmajor ? "ldc < N" : "ldc < M");
   return LVB_OK;

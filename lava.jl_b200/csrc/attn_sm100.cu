@@ -293,8 +293,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_use = (m_ref == NEG_INF) ? 0.f : m_ref;
 
+      // Exponentials first: they need only S, so they overlap the previous block's P·V.
+      const float sl = p.scale_log2;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
+        sum += p0 + p1;
+        s[c] = pack2<BF16>(p0, p1);
+      }
+
       if (j > 0) {
-        // PV of the previous block must be complete before O is rescaled or P rewritten.
+        // P·V of the previous block must be complete before O is rescaled or P rewritten.
         if (!wait_bar(&pv_done[t], (uint32_t)((j - 1) & 1), g, 22, j)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, resc)) {
@@ -309,19 +320,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_st();
         }
-        l *= alpha;
       }
-
-      const float sl = p.scale_log2;
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
-        sum += p0 + p1;
-        s[c] = pack2<BF16>(p0, p1);
-      }
-      l += sum;
+      l = l * alpha + sum;
       // P row -> shared memory, 128B-swizzled K-major: 16-byte unit u of the row goes to
       // position u ^ (row % 8) inside the row's 128-byte line, 64 keys per chunk.
 #pragma unroll
