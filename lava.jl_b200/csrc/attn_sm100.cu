@@ -152,17 +152,39 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < kDChunks; ++c)
           tma_load_4d(sQ + t * Cfg::kTileBytes + c * kChunk, &tmQ, c * 64, q0 + 128 * t, h, b,
                       q_full);
+      // Ring items in the order the MMA warp consumes them: K_0, then per block j
+      // (K_{j+1} if it exists, V_j). Slots are then released first-in first-out, so the
+      // load of K_{j+2} waits only for V_{j-1}, a whole block earlier than V_j.
       const int items = 2 * n_blocks;
       int issued = 0;
       for (int i = 0; i < items; ++i) {
+        int blk;
+        bool is_v;
+        if (i == 0) {
+          blk = 0;
+          is_v = false;
+        } else {
+          // i = 2j+1 -> K_{j+1} (j+1 < n), i = 2j+2 -> V_j; the last item is V_{n-1}.
+          const int j = (i - 1) >> 1;
+          if (i == items - 1) {
+            blk = n_blocks - 1;
+            is_v = true;
+          } else if ((i & 1) == 1) {
+            blk = j + 1;
+            is_v = false;
+          } else {
+            blk = j;
+            is_v = true;
+          }
+        }
         const int slot = i % kRing;
         const uint32_t par = (uint32_t)((i / kRing) & 1);
         if (!wait_bar(&ring_empty[slot], par ^ 1, g, 11, i)) break;
         bar_arrive_expect_tx(&ring_full[slot], Cfg::kTileBytes);
-        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+        const CUtensorMap* tm = is_v ? &tmV : &tmK;
         for (int c = 0; c < kDChunks; ++c)
-          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128, hk,
-                      b, &ring_full[slot]);
+          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, blk * 128, hk, b,
+                      &ring_full[slot]);
         issued = i + 1;
       }
       if (*abort_flag) {
@@ -209,8 +231,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mma_commit(&ring_empty[0]);
       }
       for (int j = 0; j < n_blocks && ok; ++j) {
+        // Item indices follow the producer's order: K_{j+1} = 2j+1, V_j = 2j+2 (2n-1 last).
         if (j + 1 < n_blocks) {
-          const int ik = 2 * (j + 1);
+          const int ik = 2 * j + 1;
           if (!wait_bar(&ring_full[ik % kRing], (uint32_t)((ik / kRing) & 1), g, 14, j)) break;
           for (int t = 0; t < 2 && ok; ++t) {
             if (!wait_bar(&s_free[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
@@ -221,7 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!ok) break;
           mma_commit(&ring_empty[ik % kRing]);
         }
-        const int iv = 2 * j + 1;
+        const int iv = (j + 1 < n_blocks) ? 2 * j + 2 : 2 * n_blocks - 1;
         if (!wait_bar(&ring_full[iv % kRing], (uint32_t)((iv / kRing) & 1), g, 16, j)) break;
         for (int t = 0; t < 2 && ok; ++t) {
           if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 17, j)) { ok = false; break; }
