@@ -146,6 +146,25 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
  * (cudaMallocAsync / cudaFreeAsync on `stream`). */
 int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
 
+/* lvb_gemm for callers that must not allocate device memory while they run a GEMM (a host
+ * runtime that owns all device memory through its own pool, a serving loop that forbids
+ * allocation after warm-up, work enqueued during stream capture). No counterpart in the
+ * reference: Lava has no host GEMM entry point at all; this is a second form of lvb_gemm.
+ * Same arguments, semantics and results as lvb_gemm; it calls no cudaMalloc, cudaFree,
+ * cudaMallocAsync or other device allocator. Its scratch — the device status word and the
+ * workspace for operands whose base or leading dimension is not a 16-byte multiple — is one
+ * static device array of 16 MiB + 256 bytes that every GPU loading the library keeps until
+ * the process exits. Operands needing more than 16 MiB of repack workspace are refused with
+ * LVB_ERR_UNSUPPORTED (aligned operands need none, at any size). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device current; make
+ * that first call before any stream capture. All calls share the one array and it keeps the
+ * last call's contents (the status word is cleared at the start of each call): calls that
+ * can overlap on the GPU (different streams, or different host threads) race on it and must
+ * be ordered by the caller. A wait that runs out is recorded in that shared word, not in the
+ * word lvb_device_status reads. */
+int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const void* B, void* C,
+                     void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Flash-attention forward: O = softmax(scale·Q·Kᵀ + mask)·V per (batch, query head), fp32
  * online softmax, P converted to the input type for the second product — the key-block

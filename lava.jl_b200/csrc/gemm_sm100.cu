@@ -20,6 +20,9 @@
 //   * persistent grid (one CTA per SM), tiles visited in groups of GROUP_M row-tiles so the
 //     ~148 tiles in flight share A rows and B columns in L2.
 #include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <string>
 
 #include "lvb_internal.h"
 
@@ -421,6 +424,121 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
   if (st == LVB_OK && e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaFreeAsync");
   return st;
 }
+
+// ----------------------------------------------------------------------------------------
+// GEMM without allocation (lvb_gemm_noalloc)
+//
+// Some hosts may not allocate device memory at the moment they run a GEMM: a runtime that
+// owns every byte of device memory through its own pool and forbids allocations behind its
+// back, a serving loop that must not allocate after warm-up, or code that enqueues work
+// while a stream is being captured (cudaMalloc / cudaMallocAsync are not allowed there in
+// the way lvb_gemm uses them). For them the scratch this GEMM needs lives in one
+// file-scope device array instead: the device status word at its head, and the workspace
+// that operands TMA cannot address (base or leading dimension not a 16-byte multiple) are
+// repacked into. Every GPU that loads the library keeps this array until the process exits.
+// ----------------------------------------------------------------------------------------
+constexpr size_t kNoAllocHeadBytes = 256;                   // DevStatus, padded
+constexpr size_t kNoAllocWorkspaceBytes = 16ull << 20;      // repack workspace: 16 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocHeadBytes + kNoAllocWorkspaceBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device with that device current
+// (host code may not use the symbol itself as a device pointer).
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[128];
+
+static int noalloc_scratch(int device, void** out) {
+  const char* op = "lvb_gemm_noalloc";
+  if (device < 0 || device >= 128) return fail(LVB_ERR_UNSUPPORTED, op, "device ordinal above 127");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail_cuda(e, op, "cudaGetSymbolAddress(scratch)");
+    g_noalloc_addr[device] = p;
+  }
+  *out = g_noalloc_addr[device];
+  return LVB_OK;
+}
+
+int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
+                        const void* B, void* C, cudaStream_t stream, DeviceState* dev);
+
+}  // namespace lvb
+
+extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const void* B, void* C,
+                                void* stream) {
+  using namespace lvb;
+  const char* op = "lvb_gemm_noalloc";
+  int st = lvb_gemm_check(d);
+  if (st) return st;
+  if (d->M == 0 || d->N == 0) return LVB_OK;
+  if (!C) return fail(LVB_ERR_INVALID_ARG, op, "C is NULL");
+  if (d->K > 0 && (!A || !B)) return fail(LVB_ERR_INVALID_ARG, op, "A or B is NULL");
+  const int es = dtype_size(d->a_type);
+  if (((uintptr_t)A) % es || ((uintptr_t)B) % es || ((uintptr_t)C) % dtype_size(d->c_type))
+    return fail(LVB_ERR_INVALID_ARG, op, "pointer not aligned to its element size");
+  int device = -1, major = 0, minor = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess)
+    return fail(LVB_ERR_NO_DEVICE, op, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (major != 10 || minor != 0)
+    return fail(LVB_ERR_NO_DEVICE, op, "device is not sm_100", "run on a B200");
+  void* scratch = nullptr;
+  st = noalloc_scratch(device, &scratch);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  lvb_gemm_plan plan;
+  st = lvb_gemm_plan_for(d, sms, &plan);
+  if (st) return st;
+  if (((uintptr_t)A) % 16) plan.repack_a = 1;
+  if (((uintptr_t)B) % 16) plan.repack_b = 1;
+  const long long kp = (d->K + 15) / 16 * 16;
+  const size_t bytes_a = plan.repack_a ? (size_t)d->M * kp * es : 0;
+  const size_t bytes_b = plan.repack_b ? (size_t)d->N * kp * es : 0;
+  if (d->K > 0 && bytes_a + bytes_b > kNoAllocWorkspaceBytes) {
+    char buf[200];
+    std::snprintf(buf, sizeof buf,
+                  "operands to repack need %zu bytes, above the %zu-byte static workspace",
+                  bytes_a + bytes_b, (size_t)kNoAllocWorkspaceBytes);
+    return fail(LVB_ERR_UNSUPPORTED, op, buf,
+                "pass 16-byte aligned operands with 16-byte multiple leading dimensions, or use lvb_gemm");
+  }
+
+  // The status word must start at zero for this call; the array keeps the last call's bytes.
+  DevStatus* status = reinterpret_cast<DevStatus*>(scratch);
+  e = cudaMemsetAsync(status, 0, sizeof(DevStatus), s);
+  if (e != cudaSuccess) return fail_cuda(e, op, "clearing the status word");
+  if (d->K == 0) return gemm_zero_fill(d, C, s);
+
+  DeviceState local;  // no allocation: the status word is the scratch head
+  local.device = device;
+  local.sm_count = sms;
+  local.status = status;
+  lvb_gemm_desc d2 = *d;
+  const void* a = A;
+  const void* b = B;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(scratch) + kNoAllocHeadBytes;
+  if (plan.repack_a) {
+    st = repack(A, es, d->M, d->K, d->lda, ws, kp, s);
+    if (st) return st;
+    a = ws;
+    d2.lda = kp;
+  }
+  if (plan.repack_b) {
+    st = repack(B, es, d->N, d->K, d->ldb, ws + bytes_a, kp, s);
+    if (st) return st;
+    b = ws + bytes_a;
+    d2.ldb = kp;
+  }
+  plan.repack_a = plan.repack_b = 0;
+  return gemm_launch_aligned(&d2, plan, a, b, C, s, &local);
+}
+
+namespace lvb {
 
 int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
                         const void* B, void* C, cudaStream_t stream, DeviceState* dev) {

@@ -41,7 +41,7 @@ DTYPE_SIZES = {F16: 2, BF16: 2, F32: 4, I8: 1, U8: 1, I32: 4, U32: 4}
 # Symbols include/lvb.h declares; the CPU tests check the library exports each one.
 EXPORTS = [
     "lvb_caps_sm100", "lvb_caps", "lvb_matrix_shapes", "lvb_bestshape",
-    "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm",
+    "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm", "lvb_gemm_noalloc",
     "lvb_attention_check", "lvb_attention_fwd",
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
@@ -119,6 +119,7 @@ def _load() -> C.CDLL:
         "lvb_gemm_check": ([C.POINTER(lvb_gemm_desc)], C.c_int),
         "lvb_gemm_plan_for": ([C.POINTER(lvb_gemm_desc), C.c_int32, C.POINTER(lvb_gemm_plan)], C.c_int),
         "lvb_gemm": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
+        "lvb_gemm_noalloc": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
         "lvb_attention_check": ([C.POINTER(lvb_attn_desc)], C.c_int),
         "lvb_attention_fwd": ([C.POINTER(lvb_attn_desc), P, P, P, P, P, P], C.c_int),
         "lvb_abi_version": ([], C.c_int),
