@@ -249,7 +249,7 @@ def run_reference(args, w):
 def config_of(w, n, reference=False):
     c = {"workload": f"{w['cfg']} " + (
         f"{w['ab']} GEMM M={w['M']} N={w['N']} K={w['K']} per GPU, {w['out']} C, A row-major, "
-        f"B column-major, C column-major" if w["kind"] == "gemm" else
+        f"B column-major, C row-major" if w["kind"] == "gemm" else
         f"{w['ab']} flash-attention fwd B={w['B']} Hq={w['Hq']} Hkv={w['Hkv']} S={w['S']} "
         f"D={w['D']} causal={w['causal']} per GPU")}
     c["parallelism"] = (f"row-shard x{n} (independent shards, no collective)" if w["kind"] == "gemm"
@@ -275,8 +275,10 @@ def make_gemm(torch, lvb, w, rank):
     else:
         A = (torch.rand((M, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
         Bs = (torch.rand((N, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
-    Cs = torch.empty((N, M), dtype=odt, device="cuda")        # column-major C storage
-    B, C = Bs.t(), Cs.t()
+    # C row-major: a rank's row block of the job's C is one contiguous slab, so the optional
+    # all-gather concatenates shards without a reshuffle (the kernel stores it as Cᵀ = BᵀAᵀ).
+    Cs = torch.empty((M, N), dtype=odt, device="cuda")
+    B, C = Bs.t(), Cs
 
     def step():
         lvb.gemm(C, A, B)
@@ -394,6 +396,27 @@ def run_gpu(args, w):
     h2d = sum(t.numel() * t.element_size() for t in ins)
     d2h = sum(t.numel() * t.element_size() for t in outs)
 
+    # ---- optional NCCL all-gather of the outputs (timed separately, not in `value`) ----
+    allgather = None
+    if args.allgather and world > 1:
+        from lvb.dist import allgather_rows
+        local = outs[0].reshape(outs[0].shape[0], -1)
+        for _ in range(2):
+            full = allgather_rows(local)
+        barrier()
+        e0.record(stream)
+        for _ in range(5):
+            full = allgather_rows(local)
+        e1.record(stream)
+        e1.synchronize()
+        ag_ms = max_over_ranks(e0.elapsed_time(e1) / 5)
+        nbytes = full.numel() * full.element_size()
+        allgather = {"ms": ag_ms, "bytes": nbytes,
+                     "busbw_GBs": nbytes * (world - 1) / world / (ag_ms * 1e-3) / 1e9,
+                     "how": "torch.distributed all_gather_into_tensor (NCCL over NVLink)"}
+        del full
+        barrier()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w)
@@ -427,6 +450,7 @@ def run_gpu(args, w):
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": args.steps,
+            "allgather": allgather,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -442,6 +466,8 @@ def main():
     ap.add_argument("--workload", default="gemm_f16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="lvb", choices=["lvb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--allgather", action="store_true",
+                    help="also time an NCCL all-gather of the outputs (N > 1), reported apart")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (used for short profiling runs)")
     args = ap.parse_args()

@@ -192,6 +192,18 @@ int lvb_attention_fwd(const lvb_attn_desc* d, const void* Q, const void* K, cons
                       void* O, float* lse, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Sharding across the GPUs of one box. Lava has no multi-device code; the units of this
+ * path are independent (GEMM output rows, attention (batch, kv-head) groups), so each rank
+ * computes a contiguous range and no collective is needed on the data path. Host only.
+ * ------------------------------------------------------------------------------------- */
+/* Contiguous share of `total` units for `rank` of `world`: *begin, *count. Shares are made
+ * of whole chunks of `align` units (the chunk counts of two ranks differ by at most one,
+ * lower ranks take the extra ones); the ragged last chunk (total % align) falls in the last
+ * non-empty share. */
+int lvb_shard_range(int64_t total, int32_t world, int32_t rank, int64_t align, int64_t* begin,
+                    int64_t* count);
+
+/* ---------------------------------------------------------------------------------------
  * Runtime helpers for host packages that own device buffers (Lava leaves these to its
  * runtime; LavaDeviceArray is a non-owning (ptr, dims) value, src/device/devicearray.jl:
  * 25-38).

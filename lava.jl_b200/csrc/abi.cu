@@ -480,6 +480,28 @@ int lvb_attention_fwd(const lvb_attn_desc* d, const void* Q, const void* K, cons
 }
 
 // ---------------------------------------------------------------------------------------
+// Sharding
+// ---------------------------------------------------------------------------------------
+int lvb_shard_range(int64_t total, int32_t world, int32_t rank, int64_t align, int64_t* begin,
+                    int64_t* count) {
+  const char* op = "lvb_shard_range";
+  if (!begin || !count) return fail(LVB_ERR_INVALID_ARG, op, "begin or count is NULL");
+  if (total < 0 || world <= 0 || rank < 0 || rank >= world || align <= 0)
+    return fail(LVB_ERR_INVALID_ARG, op, "need total >= 0, 0 <= rank < world, align > 0");
+  // Whole aligned chunks are dealt out as evenly as possible, lower ranks first; the ragged
+  // tail chunk (total % align) goes to the rank that owns the last chunk.
+  const int64_t chunks = (total + align - 1) / align;
+  const int64_t base = chunks / world, extra = chunks % world;
+  const int64_t c0 = rank * base + std::min<int64_t>(rank, extra);
+  const int64_t nc = base + (rank < extra ? 1 : 0);
+  int64_t b = std::min(total, c0 * align);
+  int64_t e = std::min(total, (c0 + nc) * align);
+  *begin = b;
+  *count = e - b;
+  return LVB_OK;
+}
+
+// ---------------------------------------------------------------------------------------
 // Runtime helpers
 // ---------------------------------------------------------------------------------------
 int lvb_device_count(int32_t* n) {

@@ -46,7 +46,7 @@ EXPORTS = [
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
     "lvb_stream_create", "lvb_stream_destroy", "lvb_stream_synchronize",
-    "lvb_device_status", "lvb_set_wait_timeout_ms",
+    "lvb_device_status", "lvb_set_wait_timeout_ms", "lvb_shard_range",
 ]
 
 
@@ -136,6 +136,8 @@ def _load() -> C.CDLL:
         "lvb_stream_synchronize": ([P], C.c_int),
         "lvb_device_status": ([P, C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_int32)], C.c_int),
         "lvb_set_wait_timeout_ms": ([C.c_int64], C.c_int),
+        "lvb_shard_range": ([C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.POINTER(C.c_int64),
+                             C.POINTER(C.c_int64)], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(lib, name)
