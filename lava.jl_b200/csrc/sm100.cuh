@@ -3,8 +3,8 @@
 // Every wrapper here is one PTX instruction (or a short fixed sequence) written from the
 // PTX ISA description of the Blackwell tensor-core generation: mbarriers, TMA tile loads,
 // TMEM allocation, tcgen05.mma / commit / ld, and the shared-memory and instruction
-// descriptors the MMA reads. Nothing here multicasts a TMA load: each CTA fetches its own
-// tiles, so the same code is safe when several GPUs run it side by side.
+// descriptors the MMA reads. Every TMA load here targets only the issuing CTA's own shared
+// memory and reads only this GPU's memory: each CTA fetches its own tiles.
 //
 // Bounded waits: every spin on an mbarrier goes through `wait_bar`, which gives up after a
 // wall-clock limit (%globaltimer), records where it gave up in the device status word and
@@ -110,7 +110,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const W
 }
 
 // ----------------------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled, one destination CTA)
 // ----------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
