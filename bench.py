@@ -400,13 +400,13 @@ def run_gpu(args, w):
     allgather = None
     if args.allgather and world > 1:
         from lvb.dist import allgather_rows
-        local = outs[0].reshape(outs[0].shape[0], -1)
+        shard = outs[0].reshape(outs[0].shape[0], -1)
         for _ in range(2):
-            full = allgather_rows(local)
+            full = allgather_rows(shard)
         barrier()
         e0.record(stream)
         for _ in range(5):
-            full = allgather_rows(local)
+            full = allgather_rows(shard)
         e1.record(stream)
         e1.synchronize()
         ag_ms = max_over_ranks(e0.elapsed_time(e1) / 5)
