@@ -132,6 +132,7 @@ typedef struct lvb_gemm_plan {
   int32_t instr_m, instr_n, instr_k; /* tcgen05.mma shape */
   int32_t repack_a, repack_b;        /* operand copied to an aligned stream-ordered workspace
                                         first (leading dimension or base not 16-byte aligned) */
+  int32_t cta_pair;                  /* 1: 256x256 tiles on CTA pairs (tcgen05 cta_group::2) */
 } lvb_gemm_plan;
 
 /* Validate a descriptor (host only). */

@@ -384,26 +384,35 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
   const int64_t tiles_m = (kM + 127) / 128;
   // Pick the tile width by estimated efficiency: wave quantisation times the intrinsic
   // efficiency of the narrower MMA (operand re-reads grow as BN shrinks).
-  const int cands[3] = {256, 128, 64};
-  const double intrinsic[3] = {1.0, 0.86, 0.62};
+  // Candidate 512 stands for the CTA-pair kernel (256x256 tiles, one tile per two SMs).
+  const int cands[4] = {512, 256, 128, 64};
+  const double intrinsic[4] = {1.08, 1.0, 0.86, 0.62};
   double best = -1;
   int bn = 256;
-  for (int i = 0; i < 3; ++i) {
-    const int64_t tiles = tiles_m * ((kN + cands[i] - 1) / cands[i]);
-    const int64_t waves = (tiles + sm_count - 1) / sm_count;
-    const double eff = waves ? intrinsic[i] * (double)tiles / (double)(waves * sm_count) : 0;
+  for (int i = 0; i < 4; ++i) {
+    const bool pair = cands[i] == 512;
+    const int64_t tm = pair ? (kM + 255) / 256 : tiles_m;
+    const int64_t tn = pair ? (kN + 255) / 256 : (kN + cands[i] - 1) / cands[i];
+    const int64_t slots = pair ? std::max(1, sm_count / 2) : sm_count;
+    const int64_t tiles = tm * tn;
+    const int64_t waves = (tiles + slots - 1) / slots;
+    const double eff = waves ? intrinsic[i] * (double)tiles / (double)(waves * slots) : 0;
     if (eff > best + 1e-9) { best = eff; bn = cands[i]; }
   }
-  out->tile_m = 128;
-  out->tile_n = bn;
+  const bool pair = bn == 512;
+  out->cta_pair = pair ? 1 : 0;
+  out->tile_m = pair ? 256 : 128;
+  out->tile_n = pair ? 256 : bn;
   out->tile_k = 128 / dtype_size(d->a_type);
   out->stages = gemm_stages(bn);
-  out->tiles = (int32_t)(tiles_m * ((kN + bn - 1) / bn));
-  out->ctas = std::max(1, std::min<int32_t>(out->tiles, sm_count));
+  out->tiles = (int32_t)(((kM + out->tile_m - 1) / out->tile_m) *
+                         ((kN + out->tile_n - 1) / out->tile_n));
+  out->ctas = pair ? 2 * std::max(1, std::min<int32_t>(out->tiles, std::max(1, sm_count / 2)))
+                   : std::max(1, std::min<int32_t>(out->tiles, sm_count));
   out->smem_bytes = gemm_smem_bytes(bn);
-  out->tmem_cols = 2 * bn;
-  out->instr_m = 128;
-  out->instr_n = bn;
+  out->tmem_cols = pair ? 512 : 2 * bn;
+  out->instr_m = out->tile_m;
+  out->instr_n = out->tile_n;
   out->instr_k = (d->a_type == LVB_I8 || d->a_type == LVB_U8) ? 32 : 16;
   const int es = dtype_size(d->a_type);
   out->repack_a = (d->lda * es) % 16 != 0;

@@ -266,6 +266,205 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs on two SMs computes one 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256). CTA r stages rows [128r, 128r+128) of the
+// A tile and columns [128r, 128r+128) of the B tile, so each SM streams half of B (32 KB of
+// operands per 64-deep k-block instead of 48 KB, and the shared-memory read per MMA drops by
+// a third); the even CTA issues the MMAs, both CTAs' TMA loads complete on its barrier, and
+// its commits arrive on both CTAs' barriers. Each CTA's epilogue drains its own TMEM rows.
+// ----------------------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+constexpr int kPairHalfBytes = 128 * kRowBytes;             // 16 KB: 128 rows x 128 B
+constexpr int kPairStageBytes = 2 * kPairHalfBytes;         // A half + B half
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 256 + 1024;
+
+template <int AB, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  constexpr int S = kPairStages;
+  constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
+  constexpr int kElemsPerRow = kInt ? 128 : 64;
+  constexpr int kMmaK = kInt ? 32 : 16;
+  constexpr int kMmasPerStage = kElemsPerRow / kMmaK;
+  constexpr uint32_t kDescStep = (kMmaK * (kInt ? 1 : 2)) >> 4;
+  constexpr uint32_t kIdesc =
+      kInt ? make_idesc(2, AB == AB_S8 ? 1 : 0, AB == AB_S8 ? 1 : 0, 0, 0, 256, 256)
+           : make_idesc(1, AB == AB_BF16 ? 1 : 0, AB == AB_BF16 ? 1 : 0, 0, 0, 256, 256);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* sA = smem;                        // [S][128 rows][128 B]
+  uint8_t* sB = smem + S * kPairHalfBytes;   // [S][128 rows][128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kPairStageBytes);
+  uint64_t* full = bars;            // [S]  leader: both CTAs' TMA bytes
+  uint64_t* empty = bars + S;       // [S]  both: MMA done with the stage
+  uint64_t* tfull = bars + 2 * S;   // [2]  both: accumulator ready
+  uint64_t* tempty = tfull + 2;     // [2]  leader: 8 epilogue warps released it
+  uint64_t* drain = tempty + 2;     // [1]  leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&tfull[b], 1);
+      bar_init(&tempty[b], 8);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();        // barrier.cluster is .aligned: whole warps
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t filled_mask = 0;
+    uint32_t last_phase[kPairStages] = {0};
+    bool ok = true;
+    const uint64_t pol = policy_evict_last();
+    for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!wait_bar(&empty[stage], phase ^ 1, g, 31, t)) { ok = false; break; }
+        const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+        if (leader) bar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
+        tma_load_2d_pair(sA + stage * kPairHalfBytes, &tmA, kb * kElemsPerRow,
+                         tm * 256 + 128 * (int)rank, full_leader, pol);
+        tma_load_2d_pair(sB + stage * kPairHalfBytes, &tmB, kb * kElemsPerRow,
+                         tn * 256 + 128 * (int)rank, full_leader, pol);
+        filled_mask |= 1u << stage;
+        last_phase[stage] = phase;
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok && leader) {
+      for (int s = 0; s < S; ++s)
+        if (filled_mask & (1u << s)) drain_wait(&full[s], last_phase[s], p.timeout_ns);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------- MMA issuer (even CTA of the pair) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    const uint32_t a_base = smem_u32(sA);
+    const uint32_t b_base = smem_u32(sB);
+    for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
+      if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 32, t)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * 256;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!wait_bar(&full[stage], phase, g, 33, t)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t adesc = sdesc_sw128(a_base + stage * kPairHalfBytes, 16, 1024);
+        const uint64_t bdesc = sdesc_sw128(b_base + stage * kPairHalfBytes, 16, 1024);
+#pragma unroll
+        for (int k = 0; k < kMmasPerStage; ++k) {
+          const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+          if constexpr (kInt)
+            mma_i8_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+          else
+            mma_f16_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+        }
+        const uint32_t e = smem_u32(&empty[stage]);
+        mma_commit_pair(mapa_shared(e, 0));
+        mma_commit_pair(mapa_shared(e, 1));
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      const uint32_t f = smem_u32(&tfull[acc]);
+      mma_commit_pair(mapa_shared(f, 0));
+      mma_commit_pair(mapa_shared(f, 1));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    mma_commit_pair(mapa_shared(smem_u32(drain), 0));
+    drain_wait(drain, 0, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
+    const int ew = warp - 4;
+    const int row = ew * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster_id; t < p.total_tiles; t += nclusters) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      if (!wait_bar(&tfull[acc], acc_phase, g, 34, t)) break;
+      tc_fence_after();
+      const int m = tm * 256 + 128 * (int)rank + row;
+      const bool m_ok = m < p.M;
+      const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * 256;
+      uint32_t r[32];
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        __syncwarp();
+        tmem_ld32(t_row + c * 32, r);
+        tmem_wait_ld();
+        if (c == 7) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) bar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        }
+        if (p.num_kb == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        const int n0 = tn * 256 + c * 32;
+        if (m_ok) {
+          if (n0 + 32 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+          }
+        }
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // the pair's MMAs are done with both CTAs' shared memory and TMEM
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------------------
 namespace {
@@ -306,9 +505,51 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, 
   return LVB_OK;
 }
 
+// Persistent pair kernel: one cluster of 2 per SM pair, capped by how many clusters of this
+// kernel can be resident at once (GPC boundaries can leave an SM without a partner).
+template <int AB, int OUT>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int clusters,
+                cudaStream_t stream, DeviceState* dev) {
+  auto kern = gemm_tc2_kernel<AB, OUT>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::mutex mu;
+  static int resident[128] = {0};
+  int dv = dev->device >= 0 && dev->device < 128 ? dev->device : 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (resident[dv] == 0) {
+      int n = 0;
+      cfg.gridDim = dim3(2 * std::max(1, dev->sm_count / 2));
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
+        n = std::max(1, dev->sm_count / 2);
+      cudaGetLastError();
+      resident[dv] = n;
+    }
+    clusters = std::min(clusters, resident[dv]);
+  }
+  cfg.gridDim = dim3(2 * std::max(1, clusters));
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cluster kernel launch");
+  return LVB_OK;
+}
+
 template <int AB, int OUT>
 int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
               int ctas, cudaStream_t s, DeviceState* dev) {
+  if (bn == 512) return launch_pair<AB, OUT>(ta, tb, p, ctas / 2, s, dev);
   switch (bn) {
     case 256: return launch_t<AB, OUT, 256>(ta, tb, p, ctas, s, dev);
     case 128: return launch_t<AB, OUT, 128>(ta, tb, p, ctas, s, dev);
@@ -321,6 +562,7 @@ int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmPa
 
 int gemm_smem_bytes(int bn) {
   switch (bn) {
+    case 512: return kPairSmemBytes;
     case 256: return GemmCfg<256>::kSmemBytes;
     case 128: return GemmCfg<128>::kSmemBytes;
     case 64: return GemmCfg<64>::kSmemBytes;
@@ -329,6 +571,7 @@ int gemm_smem_bytes(int bn) {
 }
 int gemm_stages(int bn) {
   switch (bn) {
+    case 512: return kPairStages;
     case 256: return GemmCfg<256>::kStages;
     case 128: return GemmCfg<128>::kStages;
     case 64: return GemmCfg<64>::kStages;
@@ -556,15 +799,16 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   int st = make_tmap_2d(&ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka, box_k,
                         kBM, "lvb_gemm");
   if (st) return st;
+  // The CTA pair stages half of the 256-column B tile per CTA.
   st = make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
-                    (uint32_t)plan.tile_n, "lvb_gemm");
+                    plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
   if (st) return st;
 
   GemmParams p;
   p.M = (int)kM;
   p.N = (int)kN;
   p.K = (int)d->K;
-  p.tiles_m = (int)((kM + kBM - 1) / kBM);
+  p.tiles_m = (int)((kM + plan.tile_m - 1) / plan.tile_m);
   p.tiles_n = (int)((kN + plan.tile_n - 1) / plan.tile_n);
   p.num_kb = (int)((d->K + box_k - 1) / box_k);
   p.total_tiles = p.tiles_m * p.tiles_n;
@@ -575,7 +819,7 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
 
   const int ab = ab_kind_of(d->a_type);
   const int out = out_kind_of(d->c_type);
-  const int bn = plan.tile_n;
+  const int bn = plan.cta_pair ? 512 : plan.tile_n;   // 512: the CTA-pair kernel
   const int ctas = plan.ctas;
   if (ab == AB_F16) {
     if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, p, ctas, stream, dev);

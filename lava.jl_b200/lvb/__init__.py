@@ -94,7 +94,7 @@ class lvb_gemm_plan(C.Structure):
                 ("tile_k", C.c_int32), ("stages", C.c_int32), ("tiles", C.c_int32),
                 ("ctas", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
                 ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32),
-                ("repack_a", C.c_int32), ("repack_b", C.c_int32)]
+                ("repack_a", C.c_int32), ("repack_b", C.c_int32), ("cta_pair", C.c_int32)]
 
 
 class lvb_attn_desc(C.Structure):

@@ -141,11 +141,16 @@ def test_gemm_without_device_fails_loudly(lvb):
 
 def test_plans(lvb):
     p = lvb.gemm_plan(8192, 8192, 8192, lvb.F16, lvb.F16)
-    assert (p.tile_m, p.tile_n, p.tile_k, p.instr_k) == (128, 256, 64, 16)
-    assert p.tiles == 64 * 32 and p.ctas == 148 and p.swap_ab == 0
-    assert p.tmem_cols == 512 and p.smem_bytes <= 232448
+    # large problems: 256x256 tiles on CTA pairs (cta_group::2), 74 pairs on 148 SMs
+    assert p.cta_pair == 1
+    assert (p.tile_m, p.tile_n, p.tile_k, p.instr_m, p.instr_k) == (256, 256, 64, 256, 16)
+    assert p.tiles == 32 * 32 and p.ctas == 148 and p.swap_ab == 0
+    assert p.tmem_cols == 512 and p.smem_bytes <= 232448 and p.stages == 6
     q = lvb.gemm_plan(8192, 8192, 8192, lvb.I8, lvb.I32)
     assert q.tile_k == 128 and q.instr_k == 32
+    # a problem with fewer 256x256 tiles than SM pairs uses 1-CTA tiles
+    s = lvb.gemm_plan(1024, 1024, 8192, lvb.F16, lvb.F32)
+    assert s.cta_pair == 0 and s.tiles > 16
     r = lvb.gemm_plan(512, 512, 512, lvb.F16, lvb.F32)
     assert r.tile_n == 64 and r.tiles == 32          # latency-bound size: more CTAs
     s = lvb.gemm_plan(1000, 300, 64, lvb.F16, lvb.F32, c_rowmajor=True)
