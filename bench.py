@@ -423,12 +423,20 @@ def run_gpu(args, w):
 
     if rank == 0:
         peaks, src = measured_peaks()
-        peak = peaks["bf16_tflops"]
+        # A timed region of a second or more of back-to-back launches is the condition the
+        # sustained figure was measured under (cuBLAS back to back for seconds, power-capped);
+        # shorter regions compare against the burst figure.
+        timed_s = ms_local * args.steps / 1e3
+        kind = "sustained" if timed_s >= 1.0 else "burst"
+        burst = peaks["bf16_tflops"]
+        peak = peaks.get("bf16_tflops_sustained", burst) if kind == "sustained" else burst
         unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
+        scale = 1.0
         if w["ab"] == "Int8":
             # no measured int8 peak: dense int8 is twice dense bf16 on this part
-            peak = 2 * peak
-            src += " (2x bf16 burst: int8 dense rate)"
+            scale = 2.0
+            src += " (2x bf16: int8 dense rate)"
+        peak, burst = peak * scale, burst * scale
         achieved = units / (ms_local * 1e-3) / 1e12
         traffic = profile_traffic(args.workload)
         line = {
@@ -440,8 +448,11 @@ def run_gpu(args, w):
             "config": config_of(w, world),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit,
                          "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{src} burst bf16_tflops (MEASURED_PEAKS.json)"
-                         if src.startswith("measured") else f"{src} 1.59 PFLOP/s"},
+                         "peak_kind": kind, "timed_region_s": timed_s,
+                         "frac_of_burst": achieved / burst,
+                         "peak_source": f"{src} bf16_tflops{'_sustained' if kind == 'sustained' else ''}"
+                                        " (MEASURED_PEAKS.json)" if src.startswith("measured")
+                                        else f"{src} (1.59 burst / 1.40 sustained PFLOP/s)"},
             "e2e": None if args.no_e2e else {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps,

@@ -385,11 +385,17 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
   // Pick the tile width by estimated efficiency: wave quantisation times the intrinsic
   // efficiency of the narrower MMA (operand re-reads grow as BN shrinks).
   // Candidate 512 stands for the CTA-pair kernel (256x256 tiles, one tile per two SMs).
+  // LVB_GEMM_TILE=512|256|128|64 forces one (tuning).
   const int cands[4] = {512, 256, 128, 64};
   const double intrinsic[4] = {1.08, 1.0, 0.86, 0.62};
+  static const int forced = [] {
+    const char* s = std::getenv("LVB_GEMM_TILE");
+    return s ? std::atoi(s) : 0;
+  }();
   double best = -1;
   int bn = 256;
   for (int i = 0; i < 4; ++i) {
+    if (forced && cands[i] != forced) continue;
     const bool pair = cands[i] == 512;
     const int64_t tm = pair ? (kM + 255) / 256 : tiles_m;
     const int64_t tn = pair ? (kN + 255) / 256 : (kN + cands[i] - 1) / cands[i];

@@ -72,6 +72,9 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 template <int D, bool BF16>
+// 10 warps: three share a scheduler on two of the four sub-partitions (16,384 registers
+// each), which caps a thread at 168 registers; the softmax threads keep a 128-key score row
+// in registers within that.
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -109,11 +112,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int q0 = pair * 256;
   const int off = p.Skv - p.Sq;  // query q sees keys <= q + off
   const int kv_blocks = (p.Skv + 127) / 128;
-  int n_blocks = kv_blocks;
+  // Key blocks per query tile: under the causal mask tile 0 stops one block earlier than
+  // tile 1 whenever its last row's keys end before tile 1's; n_blocks = max over the tiles.
+  int n_tile0 = kv_blocks, n_tile1 = kv_blocks;
   if (p.causal) {
-    const int last = min(q0 + 255, p.Sq - 1) + off;
-    n_blocks = last < 0 ? 0 : min(kv_blocks, last / 128 + 1);
+    const int last0 = min(q0 + 127, p.Sq - 1) + off;
+    const int last1 = min(q0 + 255, p.Sq - 1) + off;
+    n_tile0 = last0 < 0 ? 0 : min(kv_blocks, last0 / 128 + 1);
+    n_tile1 = last1 < 0 ? 0 : min(kv_blocks, last1 / 128 + 1);
   }
+  const int n_blocks = max(n_tile0, n_tile1);
+  auto n_tile = [&](int t) { return t ? n_tile1 : n_tile0; };
 
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
@@ -224,18 +233,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok) ok = wait_bar(&ring_full[0], 0, g, 13, 0);
       if (ok) {
         tc_fence_after();
-        issue_qk(0, 0);
-        mma_commit(&s_full[0]);
-        issue_qk(1, 0);
-        mma_commit(&s_full[1]);
+        for (int t = 0; t < 2; ++t) {
+          if (n_tile(t) == 0) continue;
+          issue_qk(t, 0);
+          mma_commit(&s_full[t]);
+        }
         mma_commit(&ring_empty[0]);
       }
       for (int j = 0; j < n_blocks && ok; ++j) {
         // Item indices follow the producer's order: K_{j+1} = 2j+1, V_j = 2j+2 (2n-1 last).
+        // A tile takes part in block j only while j < n_tile(t).
         if (j + 1 < n_blocks) {
           const int ik = 2 * j + 1;
           if (!wait_bar(&ring_full[ik % kRing], (uint32_t)((ik / kRing) & 1), g, 14, j)) break;
           for (int t = 0; t < 2 && ok; ++t) {
+            if (j + 1 >= n_tile(t)) continue;
             if (!wait_bar(&s_free[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
             tc_fence_after();
             issue_qk(t, ik % kRing);
@@ -247,6 +259,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int iv = (j + 1 < n_blocks) ? 2 * j + 2 : 2 * n_blocks - 1;
         if (!wait_bar(&ring_full[iv % kRing], (uint32_t)((iv / kRing) & 1), g, 16, j)) break;
         for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_tile(t)) continue;
           if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 17, j)) { ok = false; break; }
           tc_fence_after();
           issue_pv(t, iv % kRing, j > 0);
@@ -273,8 +286,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float l = 0.f;           // running sum of p relative to m_ref
     bool ok = true;
     const int tile_first_row = q0 + 128 * t;
+    const int nt = n_tile(t);   // key blocks this tile takes part in
 
-    for (int j = 0; j < n_blocks; ++j) {
+    for (int j = 0; j < nt; ++j) {
       if (!wait_bar(&s_full[t], (uint32_t)(j & 1), g, 21, j)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[128];
@@ -301,9 +315,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
       }
-      float mx = NEG_INF;
+      // Row max as 4 independent chains (a single chain would serialise 128 dependent
+      // max operations per row, with only two softmax warps per scheduler to hide them).
+      float mxp[4];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+      for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
+#pragma unroll
+      for (int c = 4; c < 128; c += 4)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
+      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
       const float m_new = mx * p.scale_log2;
       float alpha = 1.f;
       bool resc = false;
@@ -318,14 +339,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
       // Exponentials first: they need only S, so they overlap the previous block's P·V.
       const float sl = p.scale_log2;
-      float sum = 0.f;
+      float sump[4] = {0.f, 0.f, 0.f, 0.f};   // 4 independent chains
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
         const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
-        sum += p0 + p1;
+        sump[c & 3] += p0 + p1;
         s[c] = pack2<BF16>(p0, p1);
       }
+      const float sum = (sump[0] + sump[1]) + (sump[2] + sump[3]);
 
       if (j > 0) {
         // P·V of the previous block must be complete before O is rescaled or P rewritten.
@@ -358,7 +380,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
 
     // ---------------- epilogue: O / l -> global, lse ----------------
-    if (ok && n_blocks > 0) ok = wait_bar(&pv_done[t], (uint32_t)((n_blocks - 1) & 1), g, 23, 0);
+    if (ok && nt > 0) ok = wait_bar(&pv_done[t], (uint32_t)((nt - 1) & 1), g, 23, 0);
     if (ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -369,7 +391,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
-        if (n_blocks > 0) {
+        if (nt > 0) {
           tmem_ld32(tO + 32 * c, o);
           tmem_wait_ld();
         } else {

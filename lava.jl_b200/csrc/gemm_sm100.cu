@@ -21,6 +21,7 @@
 //     ~148 tiles in flight share A rows and B columns in L2.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -35,17 +36,33 @@ constexpr int kBM = 128;
 constexpr int kRowBytes = 128;                 // K bytes per stage row (64 f16 / 128 i8)
 constexpr int kAStageBytes = kBM * kRowBytes;  // 16 KB
 constexpr int kThreads = 256;
-constexpr int kGroupM = 16;
 
 struct GemmParams {
   int M, N, K;            // kernel space
   int tiles_m, tiles_n, num_kb;
   int total_tiles;
+  int group_m;            // row-tiles per raster group
+  int l2_mode;            // 0: A and B evict_last, 1: A evict_last / B evict_first, 2: no hint
   void* D;
   long long ldd;          // D[m + n*ldd]
   DevStatus* status;
   unsigned long long timeout_ns;
 };
+
+__device__ __forceinline__ uint64_t policy_for(int mode, bool is_a) {
+  if (mode == 2) return 0;
+  if (mode == 1 && !is_a) return policy_evict_first();
+  return policy_evict_last();
+}
+
+// TMA load with the raster's cache policy (mode 2: plain load).
+__device__ __forceinline__ void tma_load_2d_pol(void* dst, const CUtensorMap* tm, int32_t c0,
+                                                int32_t c1, uint64_t* bar, int mode, uint64_t pol) {
+  if (mode == 2)
+    tma_load_2d(dst, tm, c0, c1, bar);
+  else
+    tma_load_2d_hint(dst, tm, c0, c1, bar, pol);
+}
 
 template <int BN>
 struct GemmCfg {
@@ -58,10 +75,10 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
-  const int per_group = kGroupM * p.tiles_n;
+  const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
-  const int first_m = g * kGroupM;
-  const int gsize = min(p.tiles_m - first_m, kGroupM);
+  const int first_m = g * p.group_m;
+  const int gsize = min(p.tiles_m - first_m, p.group_m);
   const int r = t - g * per_group;
   tm = first_m + r % gsize;
   tn = r / gsize;
@@ -152,18 +169,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t filled_mask = 0;       // stages filled at least once
     uint32_t last_phase[8] = {0};
     bool ok = true;
-    const uint64_t pol_a = policy_evict_last();
-    const uint64_t pol_b = policy_evict_last();
+    const uint64_t pol_a = policy_for(p.l2_mode, true);
+    const uint64_t pol_b = policy_for(p.l2_mode, false);
     for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, p, tm, tn);
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar(&empty[stage], phase ^ 1, g, 1, t)) { ok = false; break; }
         bar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        tma_load_2d_hint(sA + stage * kAStageBytes, &tmA, kb * kElemsPerRow, tm * kBM,
-                         &full[stage], pol_a);
-        tma_load_2d_hint(sB + stage * Cfg::kBStageBytes, &tmB, kb * kElemsPerRow, tn * BN,
-                         &full[stage], pol_b);
+        tma_load_2d_pol(sA + stage * kAStageBytes, &tmA, kb * kElemsPerRow, tm * kBM,
+                        &full[stage], p.l2_mode, pol_a);
+        tma_load_2d_pol(sB + stage * Cfg::kBStageBytes, &tmB, kb * kElemsPerRow, tn * BN,
+                        &full[stage], p.l2_mode, pol_b);
         filled_mask |= 1u << stage;
         last_phase[stage] = phase;
         if (++stage == S) { stage = 0; phase ^= 1; }
@@ -347,7 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t filled_mask = 0;
     uint32_t last_phase[kPairStages] = {0};
     bool ok = true;
-    const uint64_t pol = policy_evict_last();
+    const uint64_t pol_a = p.l2_mode == 2 ? policy_evict_normal() : policy_for(p.l2_mode, true);
+    const uint64_t pol_b = p.l2_mode == 2 ? policy_evict_normal() : policy_for(p.l2_mode, false);
     for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
       int tm, tn;
       tile_coords(t, p, tm, tn);
@@ -356,9 +374,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
         if (leader) bar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
         tma_load_2d_pair(sA + stage * kPairHalfBytes, &tmA, kb * kElemsPerRow,
-                         tm * 256 + 128 * (int)rank, full_leader, pol);
+                         tm * 256 + 128 * (int)rank, full_leader, pol_a);
         tma_load_2d_pair(sB + stage * kPairHalfBytes, &tmB, kb * kElemsPerRow,
-                         tn * 256 + 128 * (int)rank, full_leader, pol);
+                         tn * 256 + 128 * (int)rank, full_leader, pol_b);
         filled_mask |= 1u << stage;
         last_phase[stage] = phase;
         if (++stage == S) { stage = 0; phase ^= 1; }
@@ -812,6 +830,18 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   p.tiles_n = (int)((kN + plan.tile_n - 1) / plan.tile_n);
   p.num_kb = (int)((d->K + box_k - 1) / box_k);
   p.total_tiles = p.tiles_m * p.tiles_n;
+  // Raster group (row-tiles per group) and L2 policy; LVB_GEMM_GROUP / LVB_GEMM_L2 override
+  // them for tuning.
+  static const int env_group = [] {
+    const char* s = std::getenv("LVB_GEMM_GROUP");
+    return s ? std::atoi(s) : 0;
+  }();
+  static const int env_l2 = [] {
+    const char* s = std::getenv("LVB_GEMM_L2");
+    return s ? std::atoi(s) : -1;
+  }();
+  p.group_m = env_group > 0 ? env_group : (plan.cta_pair ? 8 : 16);
+  p.l2_mode = (env_l2 >= 0 && env_l2 <= 2) ? env_l2 : 0;
   p.D = C;
   p.ldd = d->ldc;
   p.status = dev->status;
