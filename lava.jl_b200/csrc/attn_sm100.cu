@@ -9,18 +9,22 @@
 // then O / l stored through a clamped layout.
 //
 // How, per CTA = two 128-row query tiles of one (batch, query head):
+//   * TMEM: S_0 | S_1 | O_0 | O_1 = 512 columns. P_t (16-bit) overwrites the first 64
+//     columns of S_t once the softmax has read S_t into registers, and the P·V product
+//     takes P straight from TMEM (tcgen05.mma with the A operand in TMEM), so P never
+//     touches shared memory;
 //   * warp 8 lane 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through a
-//     3-slot ring of 128-key blocks (128B swizzle, zero fill past seq_kv);
-//   * warp 9 lane 0 (MMA): S_t = Q_t·K_jᵀ into TMEM (128×128 fp32 per tile), and
-//     O_t += P_t·V_j into TMEM (128×D fp32 per tile) with V as an MN-major B operand; the
-//     QK of block j+1 is issued as soon as a softmax group has read S_t(j), so the tensor
-//     core works on one tile while the other tile's softmax runs;
+//     5-slot ring of 128-key blocks (128B swizzle, zero fill past seq_kv);
+//   * warp 9 lane 0 (MMA): per key block j the tensor core runs PV_0(j), QK_0(j+1),
+//     PV_1(j), QK_1(j+1): while one tile's softmax works, the other tile's two products
+//     run. MMAs of one thread execute in order, so QK_t(j+1) overwriting S_t/P_t after
+//     PV_t(j) read P_t is ordered, and the commit that announces S_t(j+1) also covers
+//     PV_t(j): a softmax that sees S_t(j+1) may rescale O_t and rewrite P_t at once;
 //   * warps 0-3 / 4-7 (softmax, one warpgroup per tile): thread = query row, the whole
 //     128-key row sits in registers, so max and sum need no shuffles; exp2 in the log2
 //     domain with the scale folded in; the O rescale is lazy (only when the running max
 //     grows by more than 2^8, which keeps every p <= 256) and done in TMEM by the same
-//     warp; P goes to shared memory in the 128B-swizzled K-major layout the MMA reads;
-//   * TMEM: S_0 | S_1 | O_0 | O_1 = 512 columns.
+//     warp;
 //   * grid (query-tile pairs, batch·heads), heaviest causal pair first inside a head; the
 //     pairs of one head run side by side and share its K/V blocks in L2.
 #include <algorithm>
@@ -31,8 +35,6 @@
 namespace lvb {
 
 constexpr int kAttnThreads = 320;
-constexpr int kRing = 3;
-constexpr int kPBytes = 128 * 128 * 2;  // one P tile (128 queries x 128 keys, 16-bit)
 constexpr int kChunk = 128 * 128;       // bytes of one 128-row x 64-element swizzled chunk
 
 struct AttnParams {
@@ -49,7 +51,8 @@ template <int D>
 struct AttnCfg {
   static constexpr int kTileBytes = 128 * D * 2;  // Q tile or K/V block
   static constexpr int kQBytes = 2 * kTileBytes;
-  static constexpr int kSmem = kQBytes + kRing * kTileBytes + 2 * kPBytes + 256 + 1024;
+  static constexpr int kRing = D == 128 ? 5 : 8;
+  static constexpr int kSmem = kQBytes + kRing * kTileBytes + 256 + 1024;
 };
 
 __device__ __forceinline__ void drain_wait_a(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
@@ -71,14 +74,15 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-template <int D, bool BF16>
 // 10 warps: three share a scheduler on two of the four sub-partitions (16,384 registers
 // each), which caps a thread at 168 registers; the softmax threads keep a 128-key score row
 // in registers within that.
+template <int D, bool BF16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnCfg<D>;
+  constexpr int R = Cfg::kRing;
   constexpr int kDChunks = D / 64;
   constexpr uint32_t kFmt = BF16 ? 1 : 0;
   constexpr uint32_t kIdescQK = make_idesc(1, kFmt, kFmt, 0, 0, 128, 128);
@@ -87,18 +91,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* sQ = smem;                                   // [2][D/64 chunks][128 rows][128 B]
-  uint8_t* sRing = sQ + Cfg::kQBytes;                   // [3][D/64 chunks][128 rows][128 B]
-  uint8_t* sP = sRing + kRing * Cfg::kTileBytes;        // [2][2 chunks][128 rows][128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
+  uint8_t* sRing = sQ + Cfg::kQBytes;                   // [R][D/64 chunks][128 rows][128 B]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + R * Cfg::kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* ring_full = bars + 1;     // [3]
-  uint64_t* ring_empty = bars + 4;    // [3]
-  uint64_t* s_full = bars + 7;        // [2]
-  uint64_t* s_free = bars + 9;        // [2]
-  uint64_t* p_full = bars + 11;       // [2]
-  uint64_t* pv_done = bars + 13;      // [2]
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* ring_full = bars + 1;          // [R]
+  uint64_t* ring_empty = ring_full + R;    // [R]
+  uint64_t* s_full = ring_empty + R;       // [2] QK_t done (and every MMA before it)
+  uint64_t* p_full = s_full + 2;           // [2] softmax_t wrote P_t (128 arrivals)
+  uint64_t* pv_done = p_full + 2;          // [2] PV_t done
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -122,17 +124,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     n_tile1 = last1 < 0 ? 0 : min(kv_blocks, last1 / 128 + 1);
   }
   const int n_blocks = max(n_tile0, n_tile1);
-  auto n_tile = [&](int t) { return t ? n_tile1 : n_tile0; };
 
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
-    for (int s = 0; s < kRing; ++s) {
+    for (int s = 0; s < R; ++s) {
       bar_init(&ring_full[s], 1);
       bar_init(&ring_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       bar_init(&s_full[t], 1);
-      bar_init(&s_free[t], 128);
       bar_init(&p_full[t], 128);
       bar_init(&pv_done[t], 1);
     }
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == 8) {
     if (lane == 0 && n_blocks > 0) {
-      // ---------------- TMA producer ----------------
+      // ---------------- TMA producer: Q, then K_0, V_0, K_1, V_1, ... ----------------
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
@@ -161,45 +161,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < kDChunks; ++c)
           tma_load_4d(sQ + t * Cfg::kTileBytes + c * kChunk, &tmQ, c * 64, q0 + 128 * t, h, b,
                       q_full);
-      // Ring items in the order the MMA warp consumes them: K_0, then per block j
-      // (K_{j+1} if it exists, V_j). Slots are then released first-in first-out, so the
-      // load of K_{j+2} waits only for V_{j-1}, a whole block earlier than V_j.
       const int items = 2 * n_blocks;
       int issued = 0;
       for (int i = 0; i < items; ++i) {
-        int blk;
-        bool is_v;
-        if (i == 0) {
-          blk = 0;
-          is_v = false;
-        } else {
-          // i = 2j+1 -> K_{j+1} (j+1 < n), i = 2j+2 -> V_j; the last item is V_{n-1}.
-          const int j = (i - 1) >> 1;
-          if (i == items - 1) {
-            blk = n_blocks - 1;
-            is_v = true;
-          } else if ((i & 1) == 1) {
-            blk = j + 1;
-            is_v = false;
-          } else {
-            blk = j;
-            is_v = true;
-          }
-        }
-        const int slot = i % kRing;
-        const uint32_t par = (uint32_t)((i / kRing) & 1);
+        const int slot = i % R;
+        const uint32_t par = (uint32_t)((i / R) & 1);
         if (!wait_bar(&ring_empty[slot], par ^ 1, g, 11, i)) break;
         bar_arrive_expect_tx(&ring_full[slot], Cfg::kTileBytes);
-        const CUtensorMap* tm = is_v ? &tmV : &tmK;
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         for (int c = 0; c < kDChunks; ++c)
-          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, blk * 128, hk, b,
-                      &ring_full[slot]);
+          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128, hk,
+                      b, &ring_full[slot]);
         issued = i + 1;
       }
       if (*abort_flag) {
         drain_wait_a(q_full, 0, p.timeout_ns);
-        for (int i = max(0, issued - kRing); i < issued; ++i)
-          drain_wait_a(&ring_full[i % kRing], (uint32_t)((i / kRing) & 1), p.timeout_ns);
+        for (int i = max(0, issued - R); i < issued; ++i)
+          drain_wait_a(&ring_full[i % R], (uint32_t)((i / R) & 1), p.timeout_ns);
       }
     }
   } else if (warp == 9) {
@@ -207,7 +185,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // ---------------- MMA issuer ----------------
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t r_base = smem_u32(sRing);
-      const uint32_t p_base = smem_u32(sP);
       auto issue_qk = [&](int t, int slot) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -219,18 +196,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       auto issue_pv = [&](int t, int slot, bool acc) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA
-          const uint64_t ad =
-              sdesc_sw128(p_base + t * kPBytes + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+        for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA: P columns 8kk..8kk+7
           // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64 dims
           // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
           const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
                                           kChunk, 1024);
-          mma_f16_ss(tmem + 256 + 128 * t, ad, bd, kIdescPV, (acc || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
+                     (acc || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = wait_bar(q_full, 0, g, 12, 0);
-      if (ok) ok = wait_bar(&ring_full[0], 0, g, 13, 0);
+      auto n_tile = [&](int t) { return t ? n_tile1 : n_tile0; };
+      bool ok = wait_bar(q_full, 0, g, 12, 0) && wait_bar(&ring_full[0], 0, g, 13, 0);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < 2; ++t) {
@@ -238,35 +214,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           issue_qk(t, 0);
           mma_commit(&s_full[t]);
         }
-        mma_commit(&ring_empty[0]);
+        mma_commit(&ring_empty[0]);  // K_0 (item 0)
       }
       for (int j = 0; j < n_blocks && ok; ++j) {
-        // Item indices follow the producer's order: K_{j+1} = 2j+1, V_j = 2j+2 (2n-1 last).
-        // A tile takes part in block j only while j < n_tile(t).
-        if (j + 1 < n_blocks) {
-          const int ik = 2 * j + 1;
-          if (!wait_bar(&ring_full[ik % kRing], (uint32_t)((ik / kRing) & 1), g, 14, j)) break;
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j + 1 >= n_tile(t)) continue;
-            if (!wait_bar(&s_free[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
+        const int iv = 2 * j + 1;             // V_j
+        const int ik = 2 * j + 2;             // K_{j+1}
+        const bool next = j + 1 < n_blocks;
+        if (!wait_bar(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) break;
+        bool k_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j < n_tile(t)) {
+            if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
             tc_fence_after();
-            issue_qk(t, ik % kRing);
+            issue_pv(t, iv % R, j > 0);
+            mma_commit(&pv_done[t]);
+          }
+          if (j + 1 < n_tile(t)) {
+            if (!k_ready) {
+              if (!wait_bar(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
+                ok = false;
+                break;
+              }
+              k_ready = true;
+            }
+            issue_qk(t, ik % R);
             mma_commit(&s_full[t]);
           }
-          if (!ok) break;
-          mma_commit(&ring_empty[ik % kRing]);
-        }
-        const int iv = (j + 1 < n_blocks) ? 2 * j + 2 : 2 * n_blocks - 1;
-        if (!wait_bar(&ring_full[iv % kRing], (uint32_t)((iv / kRing) & 1), g, 16, j)) break;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j >= n_tile(t)) continue;
-          if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 17, j)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(t, iv % kRing, j > 0);
-          mma_commit(&pv_done[t]);
         }
         if (!ok) break;
-        mma_commit(&ring_empty[iv % kRing]);
+        mma_commit(&ring_empty[iv % R]);           // V_j done (both tiles)
+        if (next) {
+          if (!k_ready) {  // no tile used K_{j+1}: still consume it in order
+            if (!wait_bar(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) break;
+          }
+          mma_commit(&ring_empty[ik % R]);         // K_{j+1} done
+        }
       }
       mma_commit(drain);
       drain_wait_a(drain, 0, p.timeout_ns);
@@ -278,33 +260,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = wl * 32 + lane;               // row within the tile = TMEM lane
     const int q = q0 + 128 * t + r;             // query index
     const uint32_t lane_off = (uint32_t)(wl * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * t;
+    const uint32_t tS = tmem + lane_off + 128 * t;        // S_t, then P_t in its first 64 cols
     const uint32_t tO = tmem + lane_off + 256 + 128 * t;
-    const uint32_t p_row = smem_u32(sP) + t * kPBytes + r * 128;
     const float NEG_INF = -INFINITY;
     float m_ref = NEG_INF;   // running max (log2 domain, scale folded in)
     float l = 0.f;           // running sum of p relative to m_ref
     bool ok = true;
     const int tile_first_row = q0 + 128 * t;
-    const int nt = n_tile(t);   // key blocks this tile takes part in
+    const int nt = t ? n_tile1 : n_tile0;   // key blocks this tile takes part in
 
     for (int j = 0; j < nt; ++j) {
+      // S_t(j) ready; PV_t(j-1) (so O_t, and the P_t columns) is complete too.
       if (!wait_bar(&s_full[t], (uint32_t)(j & 1), g, 21, j)) { ok = false; break; }
       tc_fence_after();
       uint32_t s[128];
-      {
-        uint32_t (&s0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[0]);
-        uint32_t (&s1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[32]);
-        uint32_t (&s2)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[64]);
-        uint32_t (&s3)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[96]);
-        tmem_ld32(tS + 0, s0);
-        tmem_ld32(tS + 32, s1);
-        tmem_ld32(tS + 64, s2);
-        tmem_ld32(tS + 96, s3);
-      }
+      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
+      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
+      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
+      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
       tmem_wait_ld();
-      tc_fence_before();
-      bar_arrive(&s_free[t]);
 
       const int kbase = j * 128;
       const bool need_mask =
@@ -316,7 +290,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
       }
       // Row max as 4 independent chains (a single chain would serialise 128 dependent
-      // max operations per row, with only two softmax warps per scheduler to hide them).
+      // max operations per row).
       float mxp[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
@@ -337,9 +311,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_use = (m_ref == NEG_INF) ? 0.f : m_ref;
 
-      // Exponentials first: they need only S, so they overlap the previous block's P·V.
       const float sl = p.scale_log2;
-      float sump[4] = {0.f, 0.f, 0.f, 0.f};   // 4 independent chains
+      float sump[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
@@ -347,34 +320,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         sump[c & 3] += p0 + p1;
         s[c] = pack2<BF16>(p0, p1);
       }
-      const float sum = (sump[0] + sump[1]) + (sump[2] + sump[3]);
-
-      if (j > 0) {
-        // P·V of the previous block must be complete before O is rescaled or P rewritten.
-        if (!wait_bar(&pv_done[t], (uint32_t)((j - 1) & 1), g, 22, j)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
+      // P_t (64 packed columns) over the first half of S_t: the MMA's A operand.
+      tmem_st32(tS + 0, &s[0]);
+      tmem_st32(tS + 32, &s[32]);
+      if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(tO + 16 * c, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(tO + 16 * c, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st16(tO + 16 * c, o);
-          }
-          tmem_wait_st();
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st16(tO + 16 * c, o);
         }
       }
-      l = l * alpha + sum;
-      // P row -> shared memory, 128B-swizzled K-major: 16-byte unit u of the row goes to
-      // position u ^ (row % 8) inside the row's 128-byte line, 64 keys per chunk.
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const uint32_t addr = p_row + (u >> 3) * kChunk + ((((u & 7) ^ (r & 7))) << 4);
-        st_shared_v4(addr, s[4 * u], s[4 * u + 1], s[4 * u + 2], s[4 * u + 3]);
-      }
-      fence_proxy_async_smem();
+      tmem_wait_st();
+      l = l * alpha + ((sump[0] + sump[1]) + (sump[2] + sump[3]));
       tc_fence_before();
       bar_arrive(&p_full[t]);
     }
@@ -385,7 +346,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = q < p.Sq;
-      typedef __align__(16) uint32_t u4[4];
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.O) +
                       2 * ((long long)b * p.o_sb + (long long)h * p.o_sh + (long long)q * p.o_ss);
 #pragma unroll 1

@@ -7,7 +7,7 @@
 
 #include <string>
 
-#include "../../include/lvb.h"
+#include "lvb.h"   // include/ is on the compiler's include path (build.py)
 #include "sm100.cuh"
 
 namespace lvb {
