@@ -283,42 +283,71 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int kbase = j * 128;
       const bool need_mask =
           (kbase + 127 >= p.Skv) || (p.causal && kbase + 127 > tile_first_row + off);
-      if (need_mask) {
-        const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
+      const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
+      auto mask = [&]() {
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
-      }
-      // Row max as 4 independent chains (a single chain would serialise 128 dependent
-      // max operations per row).
-      float mxp[4];
+          for (int c = 0; c < 128; ++c)
+            if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
+        }
+      };
+      const float sl = p.scale_log2;
+      // p = 2^(s·scale·log2e - m) for the row, packed pairwise in place over s[0..63];
+      // returns the row sum (4 independent chains).
+      auto exps = [&](float m_use) {
+        float sump[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
-#pragma unroll
-      for (int c = 4; c < 128; c += 4)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
-      const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-      const float m_new = mx * p.scale_log2;
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
+          sump[c & 3] += p0 + p1;
+          s[c] = pack2<BF16>(p0, p1);
+        }
+        return (sump[0] + sump[1]) + (sump[2] + sump[3]);
+      };
+      mask();
+
+      // Lazy rescaling needs the block's row max only when it exceeds the running max by
+      // more than 2^8. So from the second block on, exponentiate against the running max
+      // first: a row sum <= 256 proves every p <= 2^8 and the block is done. Otherwise
+      // (or on the first block, or for a row with no key yet) the warp reloads S from TMEM,
+      // takes the true max and recomputes; a row that passed the first test recomputes the
+      // same values.
       float alpha = 1.f;
       bool resc = false;
-      if (j == 0) {
-        m_ref = m_new;
-      } else if (m_new > m_ref + 8.f) {
-        alpha = fast_exp2(m_ref - m_new);
-        m_ref = m_new;
-        resc = true;
+      float sum = 0.f;
+      bool done = false;
+      if (j > 0) {
+        sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
+        done = (m_ref != NEG_INF) && (sum <= 256.f);
       }
-      const float m_use = (m_ref == NEG_INF) ? 0.f : m_ref;
-
-      const float sl = p.scale_log2;
-      float sump[4] = {0.f, 0.f, 0.f, 0.f};
+      if (!__all_sync(0xffffffffu, done)) {
+        if (j > 0) {
+          tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
+          tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
+          tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
+          tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
+          tmem_wait_ld();
+          mask();
+        }
+        // Row max as 4 independent chains (one chain would serialise 128 dependent maxes).
+        float mxp[4];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
-        sump[c & 3] += p0 + p1;
-        s[c] = pack2<BF16>(p0, p1);
+        for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
+#pragma unroll
+        for (int c = 4; c < 128; c += 4)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
+        const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+        const float m_new = mx * sl;
+        if (j == 0) {
+          m_ref = m_new;
+        } else if (m_new > m_ref + 8.f) {
+          alpha = fast_exp2(m_ref - m_new);
+          m_ref = m_new;
+          resc = true;
+        }
+        sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
       }
       // P_t (64 packed columns) over the first half of S_t: the MMA's A operand.
       tmem_st32(tS + 0, &s[0]);
@@ -335,7 +364,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       tmem_wait_st();
-      l = l * alpha + ((sump[0] + sump[1]) + (sump[2] + sump[3]));
+      l = l * alpha + sum;
       tc_fence_before();
       bar_arrive(&p_full[t]);
     }
