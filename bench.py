@@ -284,12 +284,9 @@ def make_gemm(torch, lvb, w, rank):
         lvb.gemm(C, A, B)
     ins, outs = [A, Bs], [Cs]
 
-    def step_e2e(h_ins, h_outs):
-        A.copy_(h_ins[0], non_blocking=True)
-        Bs.copy_(h_ins[1], non_blocking=True)
-        lvb.gemm(C, A, B)
-        h_outs[0].copy_(Cs, non_blocking=True)
-    return step, step_e2e, ins, outs
+    def compute(d_ins, d_outs, stream):
+        lvb.gemm(d_outs[0], d_ins[0], d_ins[1].t(), stream=stream)
+    return step, compute, ins, outs
 
 
 def make_attn(torch, lvb, w, rank):
@@ -304,13 +301,61 @@ def make_attn(torch, lvb, w, rank):
     def step():
         lvb.attention(O, Q, K, V, causal=w["causal"])
 
-    def step_e2e(h_ins, h_outs):
-        Q.copy_(h_ins[0], non_blocking=True)
-        K.copy_(h_ins[1], non_blocking=True)
-        V.copy_(h_ins[2], non_blocking=True)
-        lvb.attention(O, Q, K, V, causal=w["causal"])
-        h_outs[0].copy_(O, non_blocking=True)
-    return step, step_e2e, [Q, K, V], [O]
+    def compute(d_ins, d_outs, stream):
+        lvb.attention(d_outs[0], d_ins[0], d_ins[1], d_ins[2], causal=w["causal"], stream=stream)
+    return step, compute, [Q, K, V], [O]
+
+
+def run_e2e(torch, compute, ins, outs, steps):
+    """Steps through the public API with host buffers: every step copies its inputs from
+    pinned host memory, runs the op and copies the result back to pinned host memory.
+    Two device buffer sets and three streams (copy-in, compute, copy-out) let step i+1's
+    upload, step i's compute and step i-1's download overlap, as a serving loop would.
+    Returns ms per step (device events around the whole sequence)."""
+    h_ins = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
+    for h, t in zip(h_ins, ins):
+        h.copy_(t)
+    sets = [([torch.empty_like(t) for t in ins], [torch.empty_like(t) for t in outs],
+             [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs])
+            for _ in range(2)]
+    s_in, s_mm, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_mm = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def one(i):
+        k = i % 2
+        d_in, d_out, h_out = sets[k]
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(ev_mm[k])          # set k's inputs consumed by step i-2
+            for d, h in zip(d_in, h_ins):
+                d.copy_(h, non_blocking=True)
+            ev_in[k].record(s_in)
+        with torch.cuda.stream(s_mm):
+            s_mm.wait_event(ev_in[k])
+            if i >= 2:
+                s_mm.wait_event(ev_out[k])         # set k's outputs downloaded by step i-2
+            compute(d_in, d_out, s_mm)
+            ev_mm[k].record(s_mm)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_mm[k])
+            for h, d in zip(h_out, d_out):
+                h.copy_(d, non_blocking=True)
+            ev_out[k].record(s_out)
+
+    for i in range(2):
+        one(i)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s_in)
+    for i in range(steps):
+        one(i)
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_mm)
+    t1.record(s_out)
+    t1.synchronize()
+    return t0.elapsed_time(t1) / steps
 
 
 def run_gpu(args, w):
@@ -336,7 +381,7 @@ def run_gpu(args, w):
         dist.barrier(device_ids=[local])
     import lvb
 
-    step, step_e2e, ins, outs = (make_gemm if w["kind"] == "gemm" else make_attn)(torch, lvb, w, rank)
+    step, compute, ins, outs = (make_gemm if w["kind"] == "gemm" else make_attn)(torch, lvb, w, rank)
     units = work_units(w)
     stream = torch.cuda.current_stream()
 
@@ -376,22 +421,11 @@ def run_gpu(args, w):
     value = units * world / (ms * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers ----
-    h_ins = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins] if not args.no_e2e else []
-    h_outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs] if not args.no_e2e else []
-    for h, t in zip(h_ins, ins):
-        h.copy_(t)
     e2e_steps = 0 if args.no_e2e else max(3, min(args.steps, 20))
     e2e_ms = float("nan")
     if e2e_steps:
-        for _ in range(2):
-            step_e2e(h_ins, h_outs)
         barrier()
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            step_e2e(h_ins, h_outs)
-        e1.record(stream)
-        e1.synchronize()
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+        e2e_ms = max_over_ranks(run_e2e(torch, compute, ins, outs, e2e_steps))
         barrier()
     h2d = sum(t.numel() * t.element_size() for t in ins)
     d2h = sum(t.numel() * t.element_size() for t in outs)
@@ -456,8 +490,9 @@ def run_gpu(args, w):
             "e2e": None if args.no_e2e else {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps,
-                    "path": "lvb Python binding -> liblvb C ABI; pinned host buffers; "
-                            "H2D inputs + kernel + D2H output per step"},
+                    "path": "lvb Python binding -> liblvb C ABI; pinned host buffers; every "
+                            "step: H2D of its inputs, the op, D2H of its output, on copy-in / "
+                            "compute / copy-out streams over two device buffer sets"},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": args.steps,

@@ -227,6 +227,12 @@ int lvb_device_status(void* stream, int32_t* code, int32_t* where, int32_t* bloc
 /* Wall-clock limit of every in-kernel wait, in milliseconds (default 2000; also read from
  * the environment variable LVB_WAIT_TIMEOUT_MS at first use). */
 int lvb_set_wait_timeout_ms(int64_t ms);
+/* Failure-path self-test: enqueue one CTA whose bounded mbarrier wait (the kind every kernel
+ * uses) can never be satisfied and runs out after `timeout_ms` (1..2000). Afterwards
+ * lvb_device_status reports LVB_ERR_TIMEOUT at wait site 99, and the context stays usable.
+ * The reference's counterpart is the exception-flag path a throwing Lava kernel takes
+ * (src/compiler/entry_wrapper.jl:199-216). */
+int lvb_selftest_wait_timeout(int32_t timeout_ms, void* stream);
 
 #ifdef __cplusplus
 }

@@ -20,7 +20,7 @@ REPO = HERE.parent
 CSRC = HERE / "csrc"
 LIBDIR = HERE / "lib"
 LIB = LIBDIR / "liblvb.so"
-SOURCES = ["abi.cu", "gemm_sm100.cu", "attn_sm100.cu"]
+SOURCES = ["abi.cu", "gemm_sm100.cu", "attn_sm100.cu", "selftest.cu"]
 HEADERS = ["sm100.cuh", "lvb_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

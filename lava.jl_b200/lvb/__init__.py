@@ -47,6 +47,7 @@ EXPORTS = [
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
     "lvb_stream_create", "lvb_stream_destroy", "lvb_stream_synchronize",
     "lvb_device_status", "lvb_set_wait_timeout_ms", "lvb_shard_range",
+    "lvb_selftest_wait_timeout",
 ]
 
 
@@ -138,6 +139,7 @@ def _load() -> C.CDLL:
         "lvb_set_wait_timeout_ms": ([C.c_int64], C.c_int),
         "lvb_shard_range": ([C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.POINTER(C.c_int64),
                              C.POINTER(C.c_int64)], C.c_int),
+        "lvb_selftest_wait_timeout": ([C.c_int32, P], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(lib, name)
@@ -384,6 +386,11 @@ def device_status(stream=None):
     code, where, block = C.c_int32(), C.c_int32(), C.c_int32()
     check(lib.lvb_device_status(_stream_ptr(stream), C.byref(code), C.byref(where), C.byref(block)))
     return code.value, where.value, block.value
+
+
+def selftest_wait_timeout(ms: int = 50, stream=None) -> None:
+    """Enqueue the failure-path self-test (a wait nothing satisfies, limited to ``ms``)."""
+    check(lib.lvb_selftest_wait_timeout(int(ms), _stream_ptr(stream)))
 
 
 def set_wait_timeout_ms(ms: int) -> None:
