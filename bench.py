@@ -45,6 +45,13 @@ WORKLOADS = {
                     seed=2, dtype="int8"),
     "gemm_bf16": dict(kind="gemm", cfg="C5-gemm", M=65536, N=8192, K=8192, ab="BFloat16",
                       out="BFloat16", seed=5, dtype="bf16"),
+    # C2 with the fused epilogue C = gelu(A·B + bias + R) (bias per column, R fp16 M×N)
+    "gemm_f16_fused": dict(kind="gemm", cfg="C2+epilogue", M=8192, N=8192, K=8192,
+                           ab="Float16", out="Float16", seed=1, dtype="f16", epilogue="gelu"),
+    # C2 with both operands MN-contiguous (A column-major, B row-major): read MN-major
+    "gemm_f16_mn": dict(kind="gemm", cfg="C2-transposed", M=8192, N=8192, K=8192,
+                        ab="Float16", out="Float16", seed=1, dtype="f16", a_rowmajor=False,
+                        b_rowmajor=True),
     "attn_f16": dict(kind="attn", cfg="C4", B=4, Hq=32, Hkv=32, S=4096, D=128, ab="Float16",
                      causal=True, seed=3, dtype="f16"),
     "attn_bf16": dict(kind="attn", cfg="C5-attn", B=8, Hq=64, Hkv=8, S=16384, D=128,
@@ -182,6 +189,13 @@ def cpu_step_factory(w, target_s: float):
         how = ("exact int8 GEMM as float64 BLAS (integer partial sums < 2^53)" if integer
                else "float32 BLAS sgemm on fp16-rounded inputs")
         sample = f"{rows} of {w['M']} rows of A: ({rows}x{K}) @ ({K}x{N}), {how}"
+        if w.get("epilogue"):
+            from oracle.gemm import ACTIVATIONS
+            act = ACTIVATIONS[w["epilogue"]]
+            bias = g.uniform(-1, 1, size=N).astype(np.float32)
+            R = g.uniform(-1, 1, size=(rows, N)).astype(np.float32)
+            sample += f", then {w['epilogue']}(. + bias + R) in float32"
+            return (lambda: act(A @ B + bias + R)), 2.0 * rows * N * K, sample
         return (lambda: A @ B), 2.0 * rows * N * K, sample
     # attention: whole (b, h) units at full sequence length
     from oracle.attention import attention_blockwise
@@ -248,8 +262,11 @@ def run_reference(args, w):
 
 def config_of(w, n, reference=False):
     c = {"workload": f"{w['cfg']} " + (
-        f"{w['ab']} GEMM M={w['M']} N={w['N']} K={w['K']} per GPU, {w['out']} C, A row-major, "
-        f"B column-major, C row-major" if w["kind"] == "gemm" else
+        f"{w['ab']} GEMM M={w['M']} N={w['N']} K={w['K']} per GPU, {w['out']} C, "
+        f"A {'row' if w.get('a_rowmajor', True) else 'column'}-major, "
+        f"B {'row' if w.get('b_rowmajor', False) else 'column'}-major, C row-major"
+        + (f", fused epilogue {w['epilogue']}(A·B + bias[n] + R), bias/R {w['out']}"
+           if w.get("epilogue") else "") if w["kind"] == "gemm" else
         f"{w['ab']} flash-attention fwd B={w['B']} Hq={w['Hq']} Hkv={w['Hkv']} S={w['S']} "
         f"D={w['D']} causal={w['causal']} per GPU")}
     c["parallelism"] = (f"row-shard x{n} (independent shards, no collective)" if w["kind"] == "gemm"
@@ -269,23 +286,40 @@ def make_gemm(torch, lvb, w, rank):
     tdt = {"Float16": torch.float16, "BFloat16": torch.bfloat16, "Int8": torch.int8}[w["ab"]]
     odt = {"Float16": torch.float16, "BFloat16": torch.bfloat16, "Float32": torch.float32,
            "Int32": torch.int32}[w["out"]]
+    a_rm, b_rm = w.get("a_rowmajor", True), w.get("b_rowmajor", False)
+    # storage shapes: A (M,K) row-major or (K,M) column-major; B (N,K) column-major or (K,N)
+    a_shape = (M, K) if a_rm else (K, M)
+    b_shape = (K, N) if b_rm else (N, K)
     if tdt == torch.int8:
-        A = torch.randint(-128, 128, (M, K), generator=gen, device="cuda", dtype=torch.int16).to(tdt)
-        Bs = torch.randint(-128, 128, (N, K), generator=gen, device="cuda", dtype=torch.int16).to(tdt)
+        As = torch.randint(-128, 128, a_shape, generator=gen, device="cuda", dtype=torch.int16).to(tdt)
+        Bs = torch.randint(-128, 128, b_shape, generator=gen, device="cuda", dtype=torch.int16).to(tdt)
     else:
-        A = (torch.rand((M, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
-        Bs = (torch.rand((N, K), generator=gen, device="cuda") * 2 - 1).to(tdt)
+        As = (torch.rand(a_shape, generator=gen, device="cuda") * 2 - 1).to(tdt)
+        Bs = (torch.rand(b_shape, generator=gen, device="cuda") * 2 - 1).to(tdt)
+    view_a = (lambda t: t) if a_rm else (lambda t: t.t())
+    view_b = (lambda t: t) if b_rm else (lambda t: t.t())
     # C row-major: a rank's row block of the job's C is one contiguous slab, so the optional
     # all-gather concatenates shards without a reshuffle (the kernel stores it as Cᵀ = BᵀAᵀ).
     Cs = torch.empty((M, N), dtype=odt, device="cuda")
-    B, C = Bs.t(), Cs
+    ins, outs = [As, Bs], [Cs]
+    act = w.get("epilogue")
+    if act:
+        bias = (torch.rand((N,), generator=gen, device="cuda") * 2 - 1).to(odt)
+        R = (torch.rand((M, N), generator=gen, device="cuda") * 2 - 1).to(odt)
+        ins += [bias, R]
+
+    def call(d_ins, d_outs, stream=None):
+        if act:
+            lvb.gemm(d_outs[0], view_a(d_ins[0]), view_b(d_ins[1]), stream=stream,
+                     bias=d_ins[2], residual=d_ins[3], activation=act)
+        else:
+            lvb.gemm(d_outs[0], view_a(d_ins[0]), view_b(d_ins[1]), stream=stream)
 
     def step():
-        lvb.gemm(C, A, B)
-    ins, outs = [A, Bs], [Cs]
+        call(ins, outs)
 
     def compute(d_ins, d_outs, stream):
-        lvb.gemm(d_outs[0], d_ins[0], d_ins[1].t(), stream=stream)
+        call(d_ins, d_outs, stream)
     return step, compute, ins, outs
 
 
@@ -451,6 +485,34 @@ def run_gpu(args, w):
         del full
         barrier()
 
+    # ---- fused epilogue: the same result as GEMM + a separate elementwise pass ----
+    unfused = None
+    if w.get("epilogue") and rank == 0:
+        import torch.nn.functional as F
+        A_, B_, bias_, R_ = ins
+        C_ = outs[0]
+        view_a = (lambda t: t) if w.get("a_rowmajor", True) else (lambda t: t.t())
+        view_b = (lambda t: t) if w.get("b_rowmajor", False) else (lambda t: t.t())
+        tanh = w["epilogue"] == "gelu"
+
+        def two_pass():
+            lvb.gemm(C_, view_a(A_), view_b(B_))
+            C_.copy_(F.gelu(C_.float() + bias_.float() + R_.float(),
+                            approximate="tanh" if tanh else "none"))
+        n_un = max(3, min(args.steps, 200))
+        for _ in range(3):
+            two_pass()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(n_un):
+            two_pass()
+        e1.record(stream)
+        e1.synchronize()
+        un_ms = e0.elapsed_time(e1) / n_un
+        unfused = {"ms_per_step": un_ms, "steps": n_un, "fused_ms_per_step": ms_local,
+                   "how": "lvb_gemm without epilogue, then torch elementwise "
+                          f"{w['epilogue']}(C + bias + R) as a second pass over C"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w)
@@ -498,6 +560,8 @@ def run_gpu(args, w):
             "gpu_launches": args.steps,
             "allgather": allgather,
         }
+        if unfused:
+            line["unfused_comparison"] = unfused
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -521,7 +585,8 @@ def main():
     if args.steps is None:
         # about 2 s of timed device work at the expected rate
         args.steps = {"gemm_f16": 2000, "gemm_f16_512": 2000, "gemm_i8": 3000,
-                      "gemm_bf16": 250, "attn_f16": 2000, "attn_bf16": 40}[args.workload]
+                      "gemm_bf16": 250, "attn_f16": 2000, "attn_bf16": 40,
+                      "gemm_f16_fused": 2000, "gemm_f16_mn": 2000}[args.workload]
         if args.impl == "reference":
             args.steps = 5
     args.warmup = max(args.warmup, 3)

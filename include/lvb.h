@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define LVB_ABI_VERSION 1
+#define LVB_ABI_VERSION 2
 
 typedef enum lvb_status {
   LVB_OK = 0,
@@ -113,8 +113,8 @@ int lvb_bestshape(int32_t ab, int32_t acc, int32_t scope, lvb_matrix_shape* out)
  * ------------------------------------------------------------------------------------- */
 typedef struct lvb_gemm_desc {
   int32_t a_type, b_type, c_type; /* lvb_dtype */
-  int32_t a_rowmajor;             /* 1: A (M×K) stored row-major (lda >= K) */
-  int32_t b_rowmajor;             /* 0: B (K×N) stored column-major (ldb >= K) */
+  int32_t a_rowmajor;             /* A (M×K): 1 row-major (lda >= K), 0 column-major (lda >= M) */
+  int32_t b_rowmajor;             /* B (K×N): 0 column-major (ldb >= K), 1 row-major (ldb >= N) */
   int32_t c_rowmajor;             /* 0: C (M×N) column-major (ldc >= M); 1: row-major (ldc >= N) */
   int64_t M, N, K;
   int64_t lda, ldb, ldc;          /* elements */
@@ -130,9 +130,12 @@ typedef struct lvb_gemm_plan {
   int32_t smem_bytes;   /* dynamic shared memory per CTA */
   int32_t tmem_cols;    /* TMEM columns allocated per CTA */
   int32_t instr_m, instr_n, instr_k; /* tcgen05.mma shape */
-  int32_t repack_a, repack_b;        /* operand copied to an aligned stream-ordered workspace
-                                        first (leading dimension or base not 16-byte aligned) */
+  int32_t repack_a, repack_b;        /* operand copied K-major into an aligned stream-ordered
+                                        workspace first (leading dimension or base not 16-byte
+                                        aligned, or an 8-bit operand stored MN-contiguous) */
   int32_t cta_pair;                  /* 1: 256x256 tiles on CTA pairs (tcgen05 cta_group::2) */
+  int32_t a_mnmajor, b_mnmajor;      /* operand read by the tensor core MN-major, in place (A
+                                        column-major / B row-major, 16-bit types) */
 } lvb_gemm_plan;
 
 /* Validate a descriptor (host only). */
@@ -141,11 +144,53 @@ int lvb_gemm_check(const lvb_gemm_desc* d);
 int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* out);
 /* Enqueue C = A·B on `stream` (on the current CUDA device). Supported pairs:
  *   F16×F16 -> F32|F16|BF16,  BF16×BF16 -> F32|F16|BF16,  I8×I8 -> I32,  U8×U8 -> U32.
- * A row-major and B column-major (both K-contiguous); C either layout; any leading
- * dimension >= the extent. An operand whose base or leading dimension is not a 16-byte
- * multiple is first repacked on the device into a stream-ordered workspace
- * (cudaMallocAsync / cudaFreeAsync on `stream`). */
+ * Every layout of A, B and C, any leading dimension >= the extent. A K-contiguous operand
+ * (A row-major, B column-major) is read K-major; an MN-contiguous one — Lava's transposing
+ * tensor view, permutation (1,0) (src/device/tensor_intrinsics.jl:212-320) — is read
+ * MN-major in place when its type is 16-bit. An operand whose base or leading dimension is
+ * not a 16-byte multiple, or an 8-bit operand stored MN-contiguous, is first copied K-major
+ * on the device into a stream-ordered workspace (cudaMallocAsync / cudaFreeAsync on
+ * `stream`). */
 int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
+
+/* Fused epilogue: C = act(A·B + bias + R), computed in fp32 and converted once to C's type.
+ * The accumulator starting from bias + residual is Lava's coopmat_add accumulator
+ * initialisation — the bias loaded at stride 0 so every column (or row) reads the same
+ * vector, the residual at its own leading dimension (src/device/coopmat_intrinsics.jl:
+ * 435-447; src/compiler/spirv/coopmat.jl:873-878) — and `act` the per-element function a
+ * GEMM applies to its accumulator with coopmat_perelement / getcomp+setcomp (coopmat_
+ * intrinsics.jl:322-331,551-593) before convert and copyto! (src/vocabulary/coopmat.jl:
+ * 166-176). Floating-point outputs only (coopmat_add is OpFAdd). */
+typedef enum lvb_activation {
+  LVB_ACT_NONE = 0,
+  LVB_ACT_RELU = 1,       /* x < 0 ? 0 : x */
+  LVB_ACT_GELU_TANH = 2,  /* 0.5x(1 + tanh(sqrt(2/pi)(x + 0.044715x^3))) */
+  LVB_ACT_GELU_ERF = 3,   /* 0.5x(1 + erf(x/sqrt(2))) */
+  LVB_ACT_SILU = 4        /* x / (1 + exp(-x)) */
+} lvb_activation;
+
+typedef enum lvb_bias_axis {
+  LVB_BIAS_PER_ROW = 0,   /* bias[i] added to row i: M elements (column-major stride-0 load) */
+  LVB_BIAS_PER_COL = 1    /* bias[j] added to column j: N elements (row-major stride-0 load) */
+} lvb_bias_axis;
+
+typedef struct lvb_epilogue {
+  const void* bias;       /* NULL: none. Contiguous vector of bias_type */
+  const void* residual;   /* NULL: none. M×N in C's layout, leading dimension ldr; may be C
+                             itself (same pointer, ldr == ldc, same type), no other overlap */
+  int64_t ldr;
+  int32_t bias_type;      /* LVB_F32 | LVB_F16 | LVB_BF16 */
+  int32_t bias_axis;      /* lvb_bias_axis */
+  int32_t residual_type;  /* LVB_F32 | LVB_F16 | LVB_BF16 */
+  int32_t activation;     /* lvb_activation */
+} lvb_epilogue;
+
+/* Validate a descriptor with its epilogue (host only; `e` may be NULL). */
+int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e);
+/* lvb_gemm with the fused epilogue `e` (NULL: exactly lvb_gemm). With K == 0 the result is
+ * act(bias + R). */
+int lvb_gemm_ex(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, const void* B,
+                void* C, void* stream);
 
 /* lvb_gemm for callers that must not allocate device memory while they run a GEMM (a host
  * runtime that owns all device memory through its own pool, a serving loop that forbids

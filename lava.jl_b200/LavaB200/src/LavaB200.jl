@@ -12,6 +12,7 @@ through Vulkan.
   round-to-nearest-even — Lava's `muladd` + `convert` + `copyto!`
   (src/vocabulary/coopmat.jl:150-203). Column-major device matrices are Julia's default;
   a row-major operand is the `transpose` of a column-major one (`Val(true)` in Lava's load).
+  Keywords `bias`, `residual`, `activation` fuse the epilogue `act(A·B + bias + residual)`.
 * `attention!(O, Q, K, V; causal, scale)` — Q/O `(E, Lq, Hq, B)`, K/V `(E, Lk, Hkv, B)`
   column-major (Lava's layout, src/device/sharedmemory.jl:73-76); GQA by head grouping.
 * `B200Array` — an owning device buffer (`lvb_malloc`/`lvb_free`); any value with
@@ -109,6 +110,15 @@ struct GemmDesc
     M::Int64; N::Int64; K::Int64
     lda::Int64; ldb::Int64; ldc::Int64
 end
+
+struct Epilogue
+    bias::Ptr{Cvoid}; residual::Ptr{Cvoid}
+    ldr::Int64
+    bias_type::Int32; bias_axis::Int32; residual_type::Int32; activation::Int32
+end
+
+const ACTIVATIONS = Dict{Symbol,Int32}(:none => 0, :relu => 1, :gelu => 2, :gelu_tanh => 2,
+                                       :gelu_erf => 3, :silu => 4)
 
 struct AttnDesc
     dtype::Int32; causal::Int32
@@ -216,20 +226,55 @@ elt(x) = eltype(x)
 elt(x::Transpose) = eltype(parent(x))
 
 """
-    gemm!(C, A, B; stream = C_NULL) -> C
+    gemm!(C, A, B; bias = nothing, bias_axis = :row, residual = nothing, activation = :none,
+          stream = C_NULL) -> C
 
-`C = A·B` on the GPU. `A` must be row-major (`transpose` of a column-major K×M device
-matrix) and `B` column-major (K×N), so both are K-contiguous; `C` may be either.
+`C = activation(A·B + bias + residual)` on the GPU. Any layout: a plain device matrix is
+column-major, its `transpose` row-major (Lava's `Val(true)` load); A column-major / B row-major
+are read MN-major by the tensor core (16-bit types) — Lava's transposing tensor view.
+
+The epilogue is optional: `bias` a device vector added per row (`bias_axis = :row`, length M,
+Lava's stride-0 accumulator load) or per column (`:col`, length N); `residual` an M×N device
+matrix in C's layout (may be `C` itself); `activation` one of `:none, :relu, :gelu`
+(tanh form), `:gelu_erf, :silu` — the accumulator initialised with `coopmat_add(bias,
+residual)` and finished with `coopmat_perelement` (src/device/coopmat_intrinsics.jl:
+435-447,551-593). Floating-point outputs only.
 """
-function gemm!(C, A, B; stream::Ptr{Cvoid} = C_NULL)
+function gemm!(C, A, B; bias = nothing, bias_axis::Symbol = :row, residual = nothing,
+               activation::Symbol = :none, stream::Ptr{Cvoid} = C_NULL)
     pa, M, K, ra, lda = layout(A)
     pb, K2, N, rb, ldb = layout(B)
     pc, M2, N2, rc, ldc = layout(C)
     (K2 == K && M2 == M && N2 == N) ||
         throw(DimensionMismatch("gemm!: ($M×$K)·($K2×$N) -> ($M2×$N2)"))
     d = GemmDesc(dtype(elt(A)), dtype(elt(B)), dtype(elt(C)), ra, rb, rc, M, N, K, lda, ldb, ldc)
-    check(ccall(sym(:lvb_gemm), Cint, (Ref{GemmDesc}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
-                d, pa, pb, pc, stream))
+    if bias === nothing && residual === nothing && activation === :none
+        check(ccall(sym(:lvb_gemm), Cint,
+                    (Ref{GemmDesc}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
+                    d, pa, pb, pc, stream))
+        return C
+    end
+    haskey(ACTIVATIONS, activation) ||
+        throw(ArgumentError("gemm!: activation must be one of $(collect(keys(ACTIVATIONS)))"))
+    bias_axis in (:row, :col) || throw(ArgumentError("gemm!: bias_axis must be :row or :col"))
+    pbias, tbias = C_NULL, Int32(2)
+    if bias !== nothing
+        length(bias) == (bias_axis === :row ? M : N) ||
+            throw(DimensionMismatch("gemm!: bias of length $(length(bias)) for $bias_axis of ($M×$N)"))
+        pbias, tbias = pointer(bias), dtype(eltype(bias))
+    end
+    pres, tres, ldr = C_NULL, Int32(2), Int64(0)
+    if residual !== nothing
+        pr, Mr, Nr, rr, ldr_ = layout(residual)
+        (Mr == M && Nr == N && rr == rc) ||
+            throw(DimensionMismatch("gemm!: residual must be ($M×$N) in C's layout"))
+        pres, tres, ldr = pr, dtype(elt(residual)), Int64(ldr_)
+    end
+    e = Epilogue(pbias, pres, ldr, tbias, Int32(bias_axis === :row ? 0 : 1), tres,
+                 ACTIVATIONS[activation])
+    check(ccall(sym(:lvb_gemm_ex), Cint,
+                (Ref{GemmDesc}, Ref{Epilogue}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
+                d, e, pa, pb, pc, stream))
     return C
 end
 

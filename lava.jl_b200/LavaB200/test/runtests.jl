@@ -39,6 +39,19 @@ using LinearAlgebra
             @test maximum(abs.(C .- ref)) <= 1e-2
             @test device_status() == (0, 0, 0)
         end
+        @testset "gemm! column-major A, fused bias + residual + relu (GPU)" begin
+            M, N, K = 256, 192, 320
+            A = Float16.(rand(Float32, M, K) .* 2 .- 1)    # column-major A: read MN-major
+            B = Float16.(rand(Float32, K, N) .* 2 .- 1)
+            bias = rand(Float32, M) .- 0.5f0
+            R = rand(Float32, M, N) .- 0.5f0
+            dC = B200Array(copy(R))                        # residual = C itself
+            gemm!(dC, B200Array(A), B200Array(B); bias = B200Array(bias), bias_axis = :row,
+                  residual = dC, activation = :relu)
+            ref = max.(Float64.(A) * Float64.(B) .+ Float64.(bias) .+ Float64.(R), 0.0)
+            @test maximum(abs.(Array(dC) .- ref)) <= 1e-2
+            @test device_status() == (0, 0, 0)
+        end
         @testset "gemm! Int8 exact (GPU)" begin
             M, N, K = 130, 70, 256
             A = rand(Int8, K, M); B = rand(Int8, K, N)

@@ -362,13 +362,48 @@ int lvb_gemm_check(const lvb_gemm_desc* d) {
                 "supported: Float16/BFloat16 -> Float32/Float16/BFloat16, Int8 -> Int32, UInt8 -> UInt32");
   }
   // An empty operand (K == 0) has no layout to check: C is the empty sum.
-  if (d->K > 0 && (d->a_rowmajor != 1 || d->b_rowmajor != 0))
-    return fail(LVB_ERR_UNSUPPORTED, op, "A must be row-major and B column-major (K contiguous)",
-                "pass the transposed product or transpose the operand");
-  if (d->K > 0 && d->lda < d->K) return fail(LVB_ERR_INVALID_ARG, op, "lda < K");
-  if (d->K > 0 && d->ldb < d->K) return fail(LVB_ERR_INVALID_ARG, op, "ldb < K");
+  if (d->K > 0) {
+    // Row-major: `stride` elements between rows; column-major: between columns
+    // (src/device/coopmat_intrinsics.jl:57-75).
+    if (d->a_rowmajor ? d->lda < d->K : d->lda < std::max<int64_t>(1, d->M))
+      return fail(LVB_ERR_INVALID_ARG, op, d->a_rowmajor ? "lda < K" : "lda < M");
+    if (d->b_rowmajor ? d->ldb < std::max<int64_t>(1, d->N) : d->ldb < d->K)
+      return fail(LVB_ERR_INVALID_ARG, op, d->b_rowmajor ? "ldb < N" : "ldb < K");
+  }
   const int64_t cmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
   if (d->ldc < cmin) return fail(LVB_ERR_INVALID_ARG, op, d->c_rowmajor ? "ldc < N" : "ldc < M");
+  return LVB_OK;
+}
+
+static bool float_type(int t) { return t == LVB_F32 || t == LVB_F16 || t == LVB_BF16; }
+
+int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e) {
+  const char* op = "lvb_gemm_ex";
+  int st = lvb_gemm_check(d);
+  if (st || !e) return st;
+  const bool any = e->bias || e->residual || e->activation != LVB_ACT_NONE;
+  if (e->activation < LVB_ACT_NONE || e->activation > LVB_ACT_SILU)
+    return fail(LVB_ERR_INVALID_ARG, op, "unknown activation");
+  if (any && !float_type(d->c_type))
+    return fail(LVB_ERR_UNSUPPORTED, op, "epilogue on an integer output",
+                "coopmat_add and the activations are floating-point");
+  if (e->bias) {
+    if (!float_type(e->bias_type))
+      return fail(LVB_ERR_UNSUPPORTED, op, "bias type must be Float32, Float16 or BFloat16");
+    if (e->bias_axis != LVB_BIAS_PER_ROW && e->bias_axis != LVB_BIAS_PER_COL)
+      return fail(LVB_ERR_INVALID_ARG, op, "bias_axis must be per-row (0) or per-column (1)");
+    if ((uintptr_t)e->bias % dtype_size(e->bias_type))
+      return fail(LVB_ERR_INVALID_ARG, op, "bias not aligned to its element size");
+  }
+  if (e->residual) {
+    if (!float_type(e->residual_type))
+      return fail(LVB_ERR_UNSUPPORTED, op, "residual type must be Float32, Float16 or BFloat16");
+    const int64_t rmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
+    if (e->ldr < rmin)
+      return fail(LVB_ERR_INVALID_ARG, op, d->c_rowmajor ? "ldr < N" : "ldr < M");
+    if ((uintptr_t)e->residual % dtype_size(e->residual_type))
+      return fail(LVB_ERR_INVALID_ARG, op, "residual not aligned to its element size");
+  }
   return LVB_OK;
 }
 
@@ -420,16 +455,19 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
   out->instr_m = out->tile_m;
   out->instr_n = out->tile_n;
   out->instr_k = (d->a_type == LVB_I8 || d->a_type == LVB_U8) ? 32 : 16;
+  // MN-contiguous operands (A column-major, B row-major) are read MN-major in place when they
+  // are 16-bit; 8-bit ones are copied K-major first.
   const int es = dtype_size(d->a_type);
-  out->repack_a = (d->lda * es) % 16 != 0;
-  out->repack_b = (d->ldb * es) % 16 != 0;
+  const bool a_mn = !d->a_rowmajor, b_mn = d->b_rowmajor != 0;
+  out->repack_a = (d->lda * es) % 16 != 0 || (a_mn && es == 1);
+  out->repack_b = (d->ldb * es) % 16 != 0 || (b_mn && es == 1);
+  out->a_mnmajor = a_mn && !out->repack_a;
+  out->b_mnmajor = b_mn && !out->repack_b;
   return LVB_OK;
 }
 
-int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream) {
-  const char* op = "lvb_gemm";
-  int st = lvb_gemm_check(d);
-  if (st) return st;
+static int gemm_enqueue(const char* op, const lvb_gemm_desc* d, const lvb_epilogue* e,
+                        const void* A, const void* B, void* C, void* stream) {
   if (d->M == 0 || d->N == 0) return LVB_OK;
   if (!C) return fail(LVB_ERR_INVALID_ARG, op, "C is NULL");
   if (d->K > 0 && (!A || !B)) return fail(LVB_ERR_INVALID_ARG, op, "A or B is NULL");
@@ -439,13 +477,27 @@ int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void
   DeviceState* dev = current_device_state(op);
   if (!dev) return LVB_ERR_NO_DEVICE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (d->K == 0) return gemm_zero_fill(d, C, s);
+  const bool epi = e && (e->bias || e->residual || e->activation != LVB_ACT_NONE);
+  if (d->K == 0) return epi ? gemm_epilogue_only(d, e, C, s) : gemm_zero_fill(d, C, s);
   lvb_gemm_plan plan;
-  st = lvb_gemm_plan_for(d, dev->sm_count, &plan);
+  int st = lvb_gemm_plan_for(d, dev->sm_count, &plan);
   if (st) return st;
-  if (((uintptr_t)A) % 16) plan.repack_a = 1;
-  if (((uintptr_t)B) % 16) plan.repack_b = 1;
-  return gemm_launch(d, plan, A, B, C, s, dev);
+  if (((uintptr_t)A) % 16) plan.repack_a = 1, plan.a_mnmajor = 0;
+  if (((uintptr_t)B) % 16) plan.repack_b = 1, plan.b_mnmajor = 0;
+  return gemm_launch(d, plan, A, B, C, epi ? e : nullptr, s, dev);
+}
+
+int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream) {
+  int st = lvb_gemm_check(d);
+  if (st) return st;
+  return gemm_enqueue("lvb_gemm", d, nullptr, A, B, C, stream);
+}
+
+int lvb_gemm_ex(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, const void* B,
+                void* C, void* stream) {
+  int st = lvb_gemm_ex_check(d, e);
+  if (st) return st;
+  return gemm_enqueue("lvb_gemm_ex", d, e, A, B, C, stream);
 }
 
 // ---------------------------------------------------------------------------------------

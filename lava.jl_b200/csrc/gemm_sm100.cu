@@ -6,8 +6,13 @@
 // (kind::f16) or int32 (kind::i8), converted with round-to-nearest-even to the output type
 // and stored with ragged edges clamped.
 //
+// Optionally with the fused epilogue D = act(A·B + (bias + R)): the accumulator started from
+// bias + residual as coopmat_add builds it, then a per-element activation
+// (src/device/coopmat_intrinsics.jl:322-331,435-447,551-593).
+//
 // How (kernel space; the host swaps A and B when the caller wants a row-major C):
-//   * operands are K-contiguous ("K-major"); a CTA owns a 128 × BN output tile;
+//   * operands are K-contiguous ("K-major"), or, for 16-bit types, MN-contiguous and read
+//     MN-major in place (Lava's transposing tensor view); a CTA owns a 128 × BN output tile;
 //   * warp 0 lane 0: TMA producer. Streams 128×128-byte A and BN×128-byte B boxes
 //     (128B swizzle, zero fill past the edges) into a STAGES-deep mbarrier ring;
 //   * warp 1 lane 0: MMA issuer. Four tcgen05.mma (128×BN×16 f16 / ×32 i8) per stage into
@@ -43,11 +48,98 @@ struct GemmParams {
   int total_tiles;
   int group_m;            // row-tiles per raster group
   int l2_mode;            // 0: A and B evict_last, 1: A evict_last / B evict_first, 2: no hint
+  int a_mn, b_mn;         // operand staged MN-major (16-bit types only): the transposed view
   void* D;
   long long ldd;          // D[m + n*ldd]
+  // Fused epilogue (kernel space): D = act(acc + (bias + R)).
+  int epi;                // any of the below present
+  int act;                // lvb_activation
+  const void* bias;       // nullable
+  int bias_kind;          // lvb_dtype of bias (F32 / F16 / BF16)
+  int bias_on_m;          // 1: bias[m] (one value per TMEM lane), 0: bias[n]
+  const void* res;        // nullable; R[m + n*ldr], may be D itself
+  int res_kind;
+  long long ldr;
   DevStatus* status;
   unsigned long long timeout_ns;
 };
+
+// Stage geometry of an MN-major 16-bit operand: 64-element (128-byte) MN chunks of 64 K
+// rows, each one TMA box; consecutive chunks 8 KB apart (the descriptor's leading byte
+// offset), 8-row K groups 1 KB apart (its stride byte offset).
+constexpr int kMnChunkBytes = 64 * 128;
+
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ __forceinline__ float load_as_f32(const void* p, int kind, long long i) {
+  if (kind == LVB_F32) return reinterpret_cast<const float*>(p)[i];
+  if (kind == LVB_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+// out[j] += X[i0 + j*stride] for j < nv. The 32 loads form one basic block ahead of the
+// conversions, so their latencies overlap.
+template <typename T>
+__device__ __forceinline__ void add_loaded32(const void* base, long long i0, long long stride,
+                                             int nv, float (&out)[32]) {
+  const T* x = reinterpret_cast<const T*>(base) + i0;
+  T v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = j < nv ? x[j * stride] : T(0.f);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) out[j] += to_f32(v[j]);
+}
+
+__device__ __forceinline__ void add_loaded32(int kind, const void* base, long long i0,
+                                             long long stride, int nv, float (&out)[32]) {
+  if (kind == LVB_F32) add_loaded32<float>(base, i0, stride, nv, out);
+  else if (kind == LVB_F16) add_loaded32<__half>(base, i0, stride, nv, out);
+  else add_loaded32<__nv_bfloat16>(base, i0, stride, nv, out);
+}
+
+// The per-element function of the epilogue (coopmat_perelement with a fixed callback).
+// gelu-tanh 0.5x(1 + tanh(u)) and silu are evaluated as x·sigmoid(t) = x / (1 + e^-t)
+// (t = 2u and t = x): the same functions, with no cancellation for negative arguments
+// (1 + tanh(u) -> 0) and a limit of -0 where e^-t overflows. gelu-erf as 0.5x·erfc(-x/√2),
+// which equals 0.5x(1 + erf(x/√2)) without the same cancellation.
+template <int ACT>
+__device__ __forceinline__ float act_fn(float v) {
+  if constexpr (ACT == LVB_ACT_RELU) {
+    return v < 0.f ? 0.f : v;  // NaN passes through, as max(x, 0) does in Julia
+  } else if constexpr (ACT == LVB_ACT_GELU_TANH) {
+    const float t = 1.5957691216057308f * fmaf(0.044715f * v, v * v, v);  // 2·sqrt(2/pi)·(...)
+    return __fdividef(v, 1.f + __expf(-t));
+  } else if constexpr (ACT == LVB_ACT_GELU_ERF) {
+    return 0.5f * v * erfcf(-0.7071067811865476f * v);
+  } else if constexpr (ACT == LVB_ACT_SILU) {
+    return __fdividef(v, 1.f + __expf(-v));
+  } else {
+    return v;
+  }
+}
+
+__device__ __forceinline__ float act_any(int act, float v) {
+  switch (act) {
+    case LVB_ACT_RELU: return act_fn<LVB_ACT_RELU>(v);
+    case LVB_ACT_GELU_TANH: return act_fn<LVB_ACT_GELU_TANH>(v);
+    case LVB_ACT_GELU_ERF: return act_fn<LVB_ACT_GELU_ERF>(v);
+    case LVB_ACT_SILU: return act_fn<LVB_ACT_SILU>(v);
+  }
+  return v;
+}
+
+// acc + (bias + R), then the activation, for one element: the accumulator started from
+// bias + residual as coopmat_add builds it (src/device/coopmat_intrinsics.jl:435-447), then
+// perelement.
+__device__ __forceinline__ float epi_value(const GemmParams& p, float acc, int m, int n,
+                                           float bias_m) {
+  float init = bias_m;
+  if (p.bias && !p.bias_on_m) init += load_as_f32(p.bias, p.bias_kind, n);
+  if (p.res) init += load_as_f32(p.res, p.res_kind, (long long)n * p.ldr + m);
+  return act_any(p.act, acc + init);
+}
 
 __device__ __forceinline__ uint64_t policy_for(int mode, bool is_a) {
   if (mode == 2) return 0;
@@ -102,6 +194,61 @@ __device__ __forceinline__ void store_out(void* D, long long idx, uint32_t bits)
   } else {
     reinterpret_cast<__nv_bfloat16*>(D)[idx] = __float2bfloat16_rn(__uint_as_float(bits));
   }
+}
+
+// v[j] = act(acc[j] + init[j]) for the 32 columns, then the clamped stores: the arithmetic is
+// straight-line code over independent elements.
+template <int OUT, int ACT>
+__device__ __forceinline__ void store_epi32(const GemmParams& p, const uint32_t (&r)[32],
+                                            const float (&init)[32], int m, int n0, int nv) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT>(__uint_as_float(r[j]) + init[j]);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < nv) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, __float_as_uint(v[j]));
+}
+
+// Store 32 columns n0.. of row m (one tcgen05.ld worth), clamped to N, with or without the
+// fused epilogue. Lanes hold consecutive m, so every column is one coalesced warp store (and
+// every residual column one coalesced warp load).
+template <int OUT>
+__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int m,
+                                            int n0, float bias_m) {
+  if (p.epi) {
+    if constexpr (OUT != OUT_I32) {
+      const int nv = min(32, p.N - n0);
+      float init[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) init[j] = bias_m;
+      if (p.bias && !p.bias_on_m) add_loaded32(p.bias_kind, p.bias, n0, 1, nv, init);
+      if (p.res) add_loaded32(p.res_kind, p.res, (long long)n0 * p.ldr + m, p.ldr, nv, init);
+      switch (p.act) {
+        case LVB_ACT_RELU: store_epi32<OUT, LVB_ACT_RELU>(p, r, init, m, n0, nv); break;
+        case LVB_ACT_GELU_TANH: store_epi32<OUT, LVB_ACT_GELU_TANH>(p, r, init, m, n0, nv); break;
+        case LVB_ACT_GELU_ERF: store_epi32<OUT, LVB_ACT_GELU_ERF>(p, r, init, m, n0, nv); break;
+        case LVB_ACT_SILU: store_epi32<OUT, LVB_ACT_SILU>(p, r, init, m, n0, nv); break;
+        default: store_epi32<OUT, LVB_ACT_NONE>(p, r, init, m, n0, nv); break;
+      }
+    }
+    return;
+  }
+  if (n0 + 32 <= p.N) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+  }
+}
+
+// Shared-memory descriptor of one operand stage and its advance per MMA, in 16-byte units.
+// K-major: rows of 128 K-bytes, 8-row groups 1 KB apart; the next MMA's K slice starts
+// kMmaK elements further along the row. MN-major: 64-element MN chunks 8 KB apart, the next
+// K slice starts 16 rows (2 KB) further down.
+__device__ __forceinline__ uint64_t stage_desc(uint32_t saddr, int mn_major) {
+  return mn_major ? sdesc_sw128(saddr, kMnChunkBytes, 1024) : sdesc_sw128(saddr, 16, 1024);
 }
 
 template <int AB, int OUT, int BN>
@@ -177,10 +324,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar(&empty[stage], phase ^ 1, g, 1, t)) { ok = false; break; }
         bar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        tma_load_2d_pol(sA + stage * kAStageBytes, &tmA, kb * kElemsPerRow, tm * kBM,
-                        &full[stage], p.l2_mode, pol_a);
-        tma_load_2d_pol(sB + stage * Cfg::kBStageBytes, &tmB, kb * kElemsPerRow, tn * BN,
-                        &full[stage], p.l2_mode, pol_b);
+        uint8_t* a_dst = sA + stage * kAStageBytes;
+        uint8_t* b_dst = sB + stage * Cfg::kBStageBytes;
+        if (!p.a_mn) {
+          tma_load_2d_pol(a_dst, &tmA, kb * kElemsPerRow, tm * kBM, &full[stage], p.l2_mode, pol_a);
+        } else {
+          for (int c = 0; c < kBM / 64; ++c)
+            tma_load_2d_pol(a_dst + c * kMnChunkBytes, &tmA, tm * kBM + 64 * c, kb * 64,
+                            &full[stage], p.l2_mode, pol_a);
+        }
+        if (!p.b_mn) {
+          tma_load_2d_pol(b_dst, &tmB, kb * kElemsPerRow, tn * BN, &full[stage], p.l2_mode, pol_b);
+        } else {
+          for (int c = 0; c < BN / 64; ++c)
+            tma_load_2d_pol(b_dst + c * kMnChunkBytes, &tmB, tn * BN + 64 * c, kb * 64,
+                            &full[stage], p.l2_mode, pol_b);
+        }
         filled_mask |= 1u << stage;
         last_phase[stage] = phase;
         if (++stage == S) { stage = 0; phase ^= 1; }
@@ -200,6 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t a_base = smem_u32(sA);
     const uint32_t b_base = smem_u32(sB);
+    // MN-major operands (16-bit only): the transpose bits of the instruction descriptor.
+    const uint32_t idesc = kIdesc | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
+    const uint32_t a_step = p.a_mn ? (16 * 128) >> 4 : kDescStep;
+    const uint32_t b_step = p.b_mn ? (16 * 128) >> 4 : kDescStep;
     for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
       if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 2, t)) { ok = false; break; }
       tc_fence_after();
@@ -207,15 +370,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar(&full[stage], phase, g, 3, t)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t adesc = sdesc_sw128(a_base + stage * kAStageBytes, 16, 1024);
-        const uint64_t bdesc = sdesc_sw128(b_base + stage * Cfg::kBStageBytes, 16, 1024);
+        const uint64_t adesc = stage_desc(a_base + stage * kAStageBytes, p.a_mn);
+        const uint64_t bdesc = stage_desc(b_base + stage * Cfg::kBStageBytes, p.b_mn);
 #pragma unroll
         for (int k = 0; k < kMmasPerStage; ++k) {
           const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
           if constexpr (kInt)
             mma_i8_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
           else
-            mma_f16_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+            mma_f16_ss(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
         }
         mma_commit(&empty[stage]);
         if (++stage == S) { stage = 0; phase ^= 1; }
@@ -241,6 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = tm * kBM + row;
       const bool m_ok = m < p.M;
+      const float bias_m =
+          (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * BN;
       uint32_t r[32];
 #pragma unroll 1
@@ -252,22 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           bar_arrive(&tempty[acc]);  // accumulator fully read: hand it back
         }
-        if (p.num_kb == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
-        }
-        const int n0 = tn * BN + c * 32;
-        if (m_ok) {
-          if (n0 + 32 <= p.N) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
-          }
-        }
+        if (m_ok) store_chunk<OUT>(p, r, m, tn * BN + c * 32, bias_m);
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
@@ -373,10 +523,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_bar(&empty[stage], phase ^ 1, g, 31, t)) { ok = false; break; }
         const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
         if (leader) bar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
-        tma_load_2d_pair(sA + stage * kPairHalfBytes, &tmA, kb * kElemsPerRow,
-                         tm * 256 + 128 * (int)rank, full_leader, pol_a);
-        tma_load_2d_pair(sB + stage * kPairHalfBytes, &tmB, kb * kElemsPerRow,
-                         tn * 256 + 128 * (int)rank, full_leader, pol_b);
+        uint8_t* a_dst = sA + stage * kPairHalfBytes;
+        uint8_t* b_dst = sB + stage * kPairHalfBytes;
+        const int a_row = tm * 256 + 128 * (int)rank;
+        const int b_row = tn * 256 + 128 * (int)rank;
+        if (!p.a_mn) {
+          tma_load_2d_pair(a_dst, &tmA, kb * kElemsPerRow, a_row, full_leader, pol_a);
+        } else {
+          tma_load_2d_pair(a_dst, &tmA, a_row, kb * 64, full_leader, pol_a);
+          tma_load_2d_pair(a_dst + kMnChunkBytes, &tmA, a_row + 64, kb * 64, full_leader, pol_a);
+        }
+        if (!p.b_mn) {
+          tma_load_2d_pair(b_dst, &tmB, kb * kElemsPerRow, b_row, full_leader, pol_b);
+        } else {
+          tma_load_2d_pair(b_dst, &tmB, b_row, kb * 64, full_leader, pol_b);
+          tma_load_2d_pair(b_dst + kMnChunkBytes, &tmB, b_row + 64, kb * 64, full_leader, pol_b);
+        }
         filled_mask |= 1u << stage;
         last_phase[stage] = phase;
         if (++stage == S) { stage = 0; phase ^= 1; }
@@ -395,6 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     const uint32_t a_base = smem_u32(sA);
     const uint32_t b_base = smem_u32(sB);
+    const uint32_t idesc = kIdesc | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
+    const uint32_t a_step = p.a_mn ? (16 * 128) >> 4 : kDescStep;
+    const uint32_t b_step = p.b_mn ? (16 * 128) >> 4 : kDescStep;
     for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
       if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 32, t)) { ok = false; break; }
       tc_fence_after();
@@ -402,15 +567,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar(&full[stage], phase, g, 33, t)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t adesc = sdesc_sw128(a_base + stage * kPairHalfBytes, 16, 1024);
-        const uint64_t bdesc = sdesc_sw128(b_base + stage * kPairHalfBytes, 16, 1024);
+        const uint64_t adesc = stage_desc(a_base + stage * kPairHalfBytes, p.a_mn);
+        const uint64_t bdesc = stage_desc(b_base + stage * kPairHalfBytes, p.b_mn);
 #pragma unroll
         for (int k = 0; k < kMmasPerStage; ++k) {
           const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
           if constexpr (kInt)
             mma_i8_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
           else
-            mma_f16_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+            mma_f16_ss_pair(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
         }
         const uint32_t e = smem_u32(&empty[stage]);
         mma_commit_pair(mapa_shared(e, 0));
@@ -439,6 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = tm * 256 + 128 * (int)rank + row;
       const bool m_ok = m < p.M;
+      const float bias_m =
+          (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * 256;
       uint32_t r[32];
 #pragma unroll 1
@@ -451,22 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) bar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
         }
-        if (p.num_kb == 0) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
-        }
-        const int n0 = tn * 256 + c * 32;
-        if (m_ok) {
-          if (n0 + 32 <= p.N) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
-          }
-        }
+        if (m_ok) store_chunk<OUT>(p, r, m, tn * 256 + c * 32, bias_m);
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
@@ -637,26 +789,78 @@ __global__ void repack_kernel(const T* __restrict__ src, long long rows, long lo
   }
 }
 
+// The same for an operand stored MN-contiguous: element (r, c) of the K-major result (r < rows
+// along M or N, c < cols along K) sits at src[c*ld + r]. 32×32 tiles through shared memory,
+// so both the read (along r) and the write (along c) are coalesced.
+template <typename T>
+__global__ void transpose_repack_kernel(const T* __restrict__ src, long long rows, long long cols,
+                                        long long ld, T* __restrict__ dst, long long dld) {
+  __shared__ T tile[32][33];
+  const long long tiles_r = (rows + 31) / 32, tiles_c = (dld + 31) / 32;
+  for (long long t = blockIdx.x; t < tiles_r * tiles_c; t += gridDim.x) {
+    const long long r0 = (t % tiles_r) * 32, c0 = (t / tiles_r) * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const long long r = r0 + threadIdx.x, c = c0 + i;
+      tile[i][threadIdx.x] = (r < rows && c < cols) ? src[c * ld + r] : T(0);
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const long long r = r0 + i, c = c0 + threadIdx.x;
+      if (r < rows && c < dld) dst[r * dld + c] = tile[threadIdx.x][i];
+    }
+    __syncthreads();
+  }
+}
+
+// Copy an operand of `rows` (M or N) × `cols` (K) into a dense K-major buffer with row
+// stride `dld`; `mn_major` when the source is stored MN-contiguous (then it is transposed).
 static int repack(const void* src, int esize, long long rows, long long cols, long long ld,
-                  void* dst, long long dld, cudaStream_t s) {
-  const long long total = rows * dld;
-  const int blocks = (int)std::min<long long>((total + 255) / 256, 8192);
-  if (esize == 1)
-    repack_kernel<uint8_t><<<blocks, 256, 0, s>>>((const uint8_t*)src, rows, cols, ld,
-                                                   (uint8_t*)dst, dld);
-  else
-    repack_kernel<uint16_t><<<blocks, 256, 0, s>>>((const uint16_t*)src, rows, cols, ld,
-                                                    (uint16_t*)dst, dld);
+                  bool mn_major, void* dst, long long dld, cudaStream_t s) {
+  if (mn_major) {
+    const long long tiles = ((rows + 31) / 32) * ((dld + 31) / 32);
+    const int blocks = (int)std::min<long long>(tiles, 8192);
+    const dim3 tb(32, 8);
+    if (esize == 1)
+      transpose_repack_kernel<uint8_t><<<blocks, tb, 0, s>>>((const uint8_t*)src, rows, cols, ld,
+                                                             (uint8_t*)dst, dld);
+    else
+      transpose_repack_kernel<uint16_t><<<blocks, tb, 0, s>>>((const uint16_t*)src, rows, cols,
+                                                              ld, (uint16_t*)dst, dld);
+  } else {
+    const long long total = rows * dld;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 8192);
+    if (esize == 1)
+      repack_kernel<uint8_t><<<blocks, 256, 0, s>>>((const uint8_t*)src, rows, cols, ld,
+                                                     (uint8_t*)dst, dld);
+    else
+      repack_kernel<uint16_t><<<blocks, 256, 0, s>>>((const uint16_t*)src, rows, cols, ld,
+                                                      (uint16_t*)dst, dld);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? LVB_OK : fail_cuda(e, "lvb_gemm", "repack launch");
 }
 
+// K == 0 with an epilogue: the accumulator is its initial value bias + R, then the
+// activation, converted and stored (kernel space, like the GEMM's own epilogue).
+template <int OUT>
+__global__ void gemm_epilogue_only_kernel(const GemmParams p) {
+  const long long total = (long long)p.M * p.N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i % p.M), n = (int)(i / p.M);
+    const float bias_m = (p.bias && p.bias_on_m) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
+    store_out<OUT>(p.D, (long long)n * p.ldd + m, __float_as_uint(epi_value(p, 0.f, m, n, bias_m)));
+  }
+}
+
 int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
-                        const void* B, void* C, cudaStream_t stream, DeviceState* dev);
+                        const void* B, void* C, const lvb_epilogue* epi, cudaStream_t stream,
+                        DeviceState* dev);
 
 int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A, const void* B,
-                void* C, cudaStream_t stream, DeviceState* dev) {
-  if (!plan.repack_a && !plan.repack_b) return gemm_launch_aligned(d, plan, A, B, C, stream, dev);
+                void* C, const lvb_epilogue* epi, cudaStream_t stream, DeviceState* dev) {
+  if (!plan.repack_a && !plan.repack_b)
+    return gemm_launch_aligned(d, plan, A, B, C, epi, stream, dev);
   // Stream-ordered workspace for the repacked operand(s); freed on the same stream.
   const int es = dtype_size(d->a_type);
   const long long kp = (d->K + 15) / 16 * 16;  // 16 elements: a 16-byte multiple for 1 and 2 bytes
@@ -666,21 +870,26 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
   cudaError_t e = cudaMallocAsync(&ws, bytes_a + bytes_b, stream);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaMallocAsync");
   lvb_gemm_desc d2 = *d;
+  lvb_gemm_plan plan2 = plan;
   const void* a = A;
   const void* b = B;
   int st = LVB_OK;
   if (plan.repack_a) {
-    st = repack(A, es, d->M, d->K, d->lda, ws, kp, stream);
+    st = repack(A, es, d->M, d->K, d->lda, !d->a_rowmajor, ws, kp, stream);
     a = ws;
     d2.lda = kp;
+    d2.a_rowmajor = 1;
+    plan2.a_mnmajor = 0;
   }
   if (st == LVB_OK && plan.repack_b) {
     void* wb = (uint8_t*)ws + bytes_a;
-    st = repack(B, es, d->N, d->K, d->ldb, wb, kp, stream);
+    st = repack(B, es, d->N, d->K, d->ldb, d->b_rowmajor != 0, wb, kp, stream);
     b = wb;
     d2.ldb = kp;
+    d2.b_rowmajor = 0;
+    plan2.b_mnmajor = 0;
   }
-  if (st == LVB_OK) st = gemm_launch_aligned(&d2, plan, a, b, C, stream, dev);
+  if (st == LVB_OK) st = gemm_launch_aligned(&d2, plan2, a, b, C, epi, stream, dev);
   e = cudaFreeAsync(ws, stream);
   if (st == LVB_OK && e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaFreeAsync");
   return st;
@@ -720,9 +929,6 @@ static int noalloc_scratch(int device, void** out) {
   *out = g_noalloc_addr[device];
   return LVB_OK;
 }
-
-int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
-                        const void* B, void* C, cudaStream_t stream, DeviceState* dev);
 
 }  // namespace lvb
 
@@ -784,25 +990,71 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   const void* b = B;
   uint8_t* ws = reinterpret_cast<uint8_t*>(scratch) + kNoAllocHeadBytes;
   if (plan.repack_a) {
-    st = repack(A, es, d->M, d->K, d->lda, ws, kp, s);
+    st = repack(A, es, d->M, d->K, d->lda, !d->a_rowmajor, ws, kp, s);
     if (st) return st;
     a = ws;
     d2.lda = kp;
+    d2.a_rowmajor = 1;
+    plan.a_mnmajor = 0;
   }
   if (plan.repack_b) {
-    st = repack(B, es, d->N, d->K, d->ldb, ws + bytes_a, kp, s);
+    st = repack(B, es, d->N, d->K, d->ldb, d->b_rowmajor != 0, ws + bytes_a, kp, s);
     if (st) return st;
     b = ws + bytes_a;
     d2.ldb = kp;
+    d2.b_rowmajor = 0;
+    plan.b_mnmajor = 0;
   }
   plan.repack_a = plan.repack_b = 0;
-  return gemm_launch_aligned(&d2, plan, a, b, C, s, &local);
+  return gemm_launch_aligned(&d2, plan, a, b, C, nullptr, s, &local);
 }
 
 namespace lvb {
 
+// Epilogue fields of the kernel parameters from the caller's description (kernel space:
+// with swap_ab the caller's rows are the kernel's n).
+static void set_epilogue(GemmParams& p, const lvb_epilogue* e, bool swap_ab) {
+  p.epi = 0;
+  p.act = LVB_ACT_NONE;
+  p.bias = p.res = nullptr;
+  p.bias_kind = p.res_kind = LVB_F32;
+  p.bias_on_m = 0;
+  p.ldr = 0;
+  if (!e) return;
+  p.act = e->activation;
+  p.bias = e->bias;
+  p.bias_kind = e->bias_type;
+  p.bias_on_m = (e->bias_axis == LVB_BIAS_PER_ROW) != swap_ab;
+  p.res = e->residual;
+  p.res_kind = e->residual_type;
+  p.ldr = e->ldr;
+  p.epi = (p.act != LVB_ACT_NONE || p.bias || p.res) ? 1 : 0;
+}
+
+int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
+                       cudaStream_t stream) {
+  GemmParams p = {};
+  const bool swap = d->c_rowmajor != 0;
+  p.M = (int)(swap ? d->N : d->M);
+  p.N = (int)(swap ? d->M : d->N);
+  p.D = C;
+  p.ldd = d->ldc;
+  set_epilogue(p, e, swap);
+  const long long total = (long long)p.M * p.N;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
+  switch (out_kind_of(d->c_type)) {
+    case OUT_F32: gemm_epilogue_only_kernel<OUT_F32><<<blocks, 256, 0, stream>>>(p); break;
+    case OUT_F16: gemm_epilogue_only_kernel<OUT_F16><<<blocks, 256, 0, stream>>>(p); break;
+    case OUT_BF16: gemm_epilogue_only_kernel<OUT_BF16><<<blocks, 256, 0, stream>>>(p); break;
+    default: return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm_ex", "epilogue on an integer output");
+  }
+  cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? LVB_OK : fail_cuda(err, "lvb_gemm_ex", "epilogue launch");
+}
+
 int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
-                        const void* B, void* C, cudaStream_t stream, DeviceState* dev) {
+                        const void* B, void* C, const lvb_epilogue* epi, cudaStream_t stream,
+                        DeviceState* dev) {
   const int esize = dtype_size(d->a_type);
   // Kernel space: rows of "A" are the lane (contiguous-store) dimension.
   const void* kA = plan.swap_ab ? B : A;
@@ -811,18 +1063,30 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   const int64_t kN = plan.swap_ab ? d->M : d->N;
   const int64_t ldka = plan.swap_ab ? d->ldb : d->lda;
   const int64_t ldkb = plan.swap_ab ? d->lda : d->ldb;
+  // Operands the tensor core reads MN-major (16-bit only; the planner repacks 8-bit ones).
+  const int ka_mn = plan.swap_ab ? plan.b_mnmajor : plan.a_mnmajor;
+  const int kb_mn = plan.swap_ab ? plan.a_mnmajor : plan.b_mnmajor;
   const uint32_t box_k = 128 / esize;
 
   CUtensorMap ta, tb;
-  int st = make_tmap_2d(&ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka, box_k,
-                        kBM, "lvb_gemm");
+  // K-major: rows of K elements, boxes of 128 K-bytes × tile rows. MN-major: rows of MN
+  // elements (one per k), boxes of 64 MN elements × 64 k.
+  int st = ka_mn ? make_tmap_2d(&ta, kA, esize, (uint64_t)kM, (uint64_t)d->K, (uint64_t)ldka, 64,
+                                64, "lvb_gemm")
+                 : make_tmap_2d(&ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka,
+                                box_k, kBM, "lvb_gemm");
   if (st) return st;
   // The CTA pair stages half of the 256-column B tile per CTA.
-  st = make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
-                    plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
+  st = kb_mn ? make_tmap_2d(&tb, kB, esize, (uint64_t)kN, (uint64_t)d->K, (uint64_t)ldkb, 64, 64,
+                            "lvb_gemm")
+             : make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
+                            plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
   if (st) return st;
 
   GemmParams p;
+  p.a_mn = ka_mn;
+  p.b_mn = kb_mn;
+  set_epilogue(p, epi, plan.swap_ab != 0);
   p.M = (int)kM;
   p.N = (int)kN;
   p.K = (int)d->K;

@@ -57,9 +57,13 @@ int dtype_size(int dt);
 const char* dtype_name(int dt);
 
 // ---- GEMM (gemm_sm100.cu) ----
-struct GemmKernelArgs;
+// `epi` is NULL for a plain GEMM.
 int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
-                const void* B, void* C, cudaStream_t stream, DeviceState* dev);
+                const void* B, void* C, const lvb_epilogue* epi, cudaStream_t stream,
+                DeviceState* dev);
+// K == 0 with an epilogue: C = act(bias + R).
+int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
+                       cudaStream_t stream);
 
 // ---- attention (attn_sm100.cu) ----
 int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,

@@ -33,6 +33,10 @@ LIB_PATH = Path(os.environ.get("LVB_LIBRARY", _HERE.parent / "lib" / "liblvb.so"
 LVB_OK, LVB_ERR_INVALID_ARG, LVB_ERR_UNSUPPORTED, LVB_ERR_CUDA = 0, 1, 2, 3
 LVB_ERR_TIMEOUT, LVB_ERR_NCCL, LVB_ERR_NO_DEVICE = 4, 5, 6
 F16, BF16, F32, I8, U8, I32, U32 = range(7)
+ACT_NONE, ACT_RELU, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SILU = range(5)
+ACTIVATIONS = {None: ACT_NONE, "none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU_TANH,
+               "gelu_tanh": ACT_GELU_TANH, "gelu_erf": ACT_GELU_ERF, "silu": ACT_SILU}
+BIAS_PER_ROW, BIAS_PER_COL = 0, 1
 SUBGROUP_SCOPE, WORKGROUP_SCOPE = 0, 1
 DTYPE_NAMES = {F16: "Float16", BF16: "BFloat16", F32: "Float32", I8: "Int8", U8: "UInt8",
                I32: "Int32", U32: "UInt32"}
@@ -42,6 +46,7 @@ DTYPE_SIZES = {F16: 2, BF16: 2, F32: 4, I8: 1, U8: 1, I32: 4, U32: 4}
 EXPORTS = [
     "lvb_caps_sm100", "lvb_caps", "lvb_matrix_shapes", "lvb_bestshape",
     "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm", "lvb_gemm_noalloc",
+    "lvb_gemm_ex_check", "lvb_gemm_ex",
     "lvb_attention_check", "lvb_attention_fwd",
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
@@ -95,7 +100,14 @@ class lvb_gemm_plan(C.Structure):
                 ("tile_k", C.c_int32), ("stages", C.c_int32), ("tiles", C.c_int32),
                 ("ctas", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
                 ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32),
-                ("repack_a", C.c_int32), ("repack_b", C.c_int32), ("cta_pair", C.c_int32)]
+                ("repack_a", C.c_int32), ("repack_b", C.c_int32), ("cta_pair", C.c_int32),
+                ("a_mnmajor", C.c_int32), ("b_mnmajor", C.c_int32)]
+
+
+class lvb_epilogue(C.Structure):
+    _fields_ = [("bias", C.c_void_p), ("residual", C.c_void_p), ("ldr", C.c_int64),
+                ("bias_type", C.c_int32), ("bias_axis", C.c_int32),
+                ("residual_type", C.c_int32), ("activation", C.c_int32)]
 
 
 class lvb_attn_desc(C.Structure):
@@ -121,6 +133,8 @@ def _load() -> C.CDLL:
         "lvb_gemm_plan_for": ([C.POINTER(lvb_gemm_desc), C.c_int32, C.POINTER(lvb_gemm_plan)], C.c_int),
         "lvb_gemm": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
         "lvb_gemm_noalloc": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
+        "lvb_gemm_ex_check": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue)], C.c_int),
+        "lvb_gemm_ex": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue), P, P, P, P], C.c_int),
         "lvb_attention_check": ([C.POINTER(lvb_attn_desc)], C.c_int),
         "lvb_attention_fwd": ([C.POINTER(lvb_attn_desc), P, P, P, P, P, P], C.c_int),
         "lvb_abi_version": ([], C.c_int),
@@ -322,19 +336,61 @@ def _stream_ptr(stream) -> Optional[int]:
     return stream.cuda_stream
 
 
-def gemm(C_, A, B, stream=None, c_type: Optional[int] = None):
+def epilogue(C_, bias=None, bias_axis: str = "col", residual=None, activation=None) -> lvb_epilogue:
+    """The ``lvb_epilogue`` for ``C = act(A·B + bias + residual)``: ``bias`` a contiguous
+    vector added per column (``bias_axis="col"``, N elements) or per row (``"row"``, M
+    elements); ``residual`` an M×N tensor in C's layout (it may be C itself)."""
+    e = lvb_epilogue()
+    if activation not in ACTIVATIONS:
+        raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm_ex: unknown activation {activation!r}")
+    e.activation = ACTIVATIONS[activation]
+    if bias is not None:
+        if bias.dim() != 1 or bias.stride(0) != 1:
+            raise LavaError(LVB_ERR_INVALID_ARG, "lvb_gemm_ex: bias must be a contiguous vector")
+        want = C_.shape[1] if bias_axis == "col" else C_.shape[0]
+        if bias.shape[0] != want:
+            raise LavaError(LVB_ERR_INVALID_ARG,
+                            f"lvb_gemm_ex: bias has {bias.shape[0]} elements, needs {want}")
+        e.bias = bias.data_ptr()
+        e.bias_type = dtype_of(bias)
+        e.bias_axis = BIAS_PER_COL if bias_axis == "col" else BIAS_PER_ROW
+    if residual is not None:
+        if tuple(residual.shape) != tuple(C_.shape):
+            raise LavaError(LVB_ERR_INVALID_ARG, "lvb_gemm_ex: residual must have C's shape")
+        rrm, ldr = _layout2d(residual, "residual")
+        crm, _ = _layout2d(C_, "C")
+        if rrm != crm and min(C_.shape) > 1:
+            raise LavaError(LVB_ERR_UNSUPPORTED, "lvb_gemm_ex: residual must have C's layout")
+        e.residual = residual.data_ptr()
+        e.residual_type = dtype_of(residual)
+        e.ldr = ldr
+    return e
+
+
+def gemm(C_, A, B, stream=None, c_type: Optional[int] = None, bias=None, bias_axis="col",
+         residual=None, activation=None):
     """``gemm!(C, A, B)``: C = A·B on the GPU (torch CUDA tensors, logical shapes
     (M,K)·(K,N) -> (M,N)); enqueued on ``stream`` (default: torch's current stream).
     ``c_type`` overrides the component type read from C (e.g. U32 held in an int32
-    tensor)."""
+    tensor). With ``bias``, ``residual`` or ``activation`` the fused epilogue runs:
+    C = act(A·B + bias + residual) (``lvb_gemm_ex``)."""
     d = gemm_desc(C_, A, B, c_type)
-    check(lib.lvb_gemm(C.byref(d), A.data_ptr(), B.data_ptr(), C_.data_ptr(), _stream_ptr(stream)))
+    if bias is None and residual is None and activation in (None, "none"):
+        check(lib.lvb_gemm(C.byref(d), A.data_ptr(), B.data_ptr(), C_.data_ptr(),
+                           _stream_ptr(stream)))
+        return C_
+    e = epilogue(C_, bias, bias_axis, residual, activation)
+    check(lib.lvb_gemm_ex(C.byref(d), C.byref(e), A.data_ptr(), B.data_ptr(), C_.data_ptr(),
+                          _stream_ptr(stream)))
     return C_
 
 
-def gemm_plan(M, N, K, a_type=F16, c_type=F32, c_rowmajor=False, sm_count=148) -> lvb_gemm_plan:
-    d = lvb_gemm_desc(a_type, a_type, c_type, 1, 0, int(c_rowmajor), M, N, K,
-                      max(K, 1), max(K, 1), max(N if c_rowmajor else M, 1))
+def gemm_plan(M, N, K, a_type=F16, c_type=F32, c_rowmajor=False, sm_count=148,
+              a_rowmajor=True, b_rowmajor=False) -> lvb_gemm_plan:
+    lda = max(K if a_rowmajor else M, 1)
+    ldb = max(N if b_rowmajor else K, 1)
+    d = lvb_gemm_desc(a_type, a_type, c_type, int(a_rowmajor), int(b_rowmajor), int(c_rowmajor),
+                      M, N, K, lda, ldb, max(N if c_rowmajor else M, 1))
     p = lvb_gemm_plan()
     check(lib.lvb_gemm_plan_for(C.byref(d), sm_count, C.byref(p)))
     return p

@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .vocab import (coopmat_convert, coopmat_muladd, tensor_load_clamped,
+from .vocab import (coopmat_add, coopmat_convert, coopmat_load, coopmat_muladd, tensor_load_clamped,
                     tensor_store_clamped, round_bf16)
 
 FLOAT_OUT = ("Float32", "Float16", "BFloat16")
@@ -112,3 +112,55 @@ def sgemm_cpu(A32: np.ndarray, B32: np.ndarray) -> np.ndarray:
 
 __all__ = ["gemm_ref", "gemm_tiled", "rel_frobenius", "max_abs", "ulp_distance_f16",
            "ulp_distance_bf16", "sgemm_cpu", "round_bf16", "to_float64"]
+
+
+# ---- fused epilogue ------------------------------------------------------------------
+# The per-element functions a GEMM applies to its accumulator with coopmat_perelement (or
+# getcomp/setcomp over coopmat_length) before convert + copyto!
+# (src/device/coopmat_intrinsics.jl:322-331,551-593), in float64.
+def _erf(x: np.ndarray) -> np.ndarray:
+    from scipy.special import erf
+    return erf(x)
+
+
+def _silu(x: np.ndarray) -> np.ndarray:
+    with np.errstate(over="ignore"):
+        return x / (1.0 + np.exp(-x))
+
+
+ACTIVATIONS = {
+    None: lambda x: x,
+    "relu": lambda x: np.where(x < 0, 0.0, x),
+    "gelu": lambda x: 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3))),
+    "gelu_erf": lambda x: 0.5 * x * (1.0 + _erf(x / np.sqrt(2.0))),
+    "silu": _silu,
+}
+ACTIVATION_SLOPE = {None: 1.0, "relu": 1.0, "gelu": 1.13, "gelu_erf": 1.13, "silu": 1.1}
+
+
+def epilogue_init(M: int, N: int, bias=None, bias_axis: str = "col", residual=None) -> np.ndarray:
+    """The accumulator a fused GEMM starts from: coopmat_add of the bias read at stride 0
+    (per row: column-major load, every column reads the same M-vector; per column: row-major
+    load) and the residual, both as Float32 accumulator matrices
+    (src/device/coopmat_intrinsics.jl:435-447; src/compiler/spirv/coopmat.jl:873-878)."""
+    init = np.zeros((M, N), dtype=np.float32)
+    if bias is not None:
+        b = np.asarray(bias, dtype=np.float32)
+        smear = coopmat_load(b, 1, 0, M, N, rowmajor=(bias_axis == "col"))
+        init = coopmat_add(init, smear)
+    if residual is not None:
+        init = coopmat_add(init, np.asarray(residual, dtype=np.float32))
+    return init
+
+
+def gemm_epilogue_ref(A: np.ndarray, B: np.ndarray, out: str, bias=None, bias_axis: str = "col",
+                      residual=None, act=None, rounded: bool = True):
+    """C = act(A·B + bias + residual): the product in float64 onto the Float32 initial
+    accumulator (``epilogue_init``), the activation in float64, one conversion to ``out``
+    (or the unrounded float64 value with ``rounded=False``). Bias and residual are given
+    as the values of their stored type."""
+    M, N = A.shape[0], B.shape[1]
+    init = epilogue_init(M, N, bias, bias_axis, residual).astype(np.float64)
+    pre = A.astype(np.float64) @ B.astype(np.float64) + init
+    val = ACTIVATIONS[act](pre)
+    return coopmat_convert(val, out) if rounded else val

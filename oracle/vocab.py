@@ -106,6 +106,20 @@ def coopmat_muladd(a: np.ndarray, b: np.ndarray, c: np.ndarray) -> np.ndarray:
     return (a.astype(np.float64) @ b.astype(np.float64) + c.astype(np.float64)).astype(c.dtype)
 
 
+def coopmat_add(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """coopmat_add(a, b): component-wise OpFAdd of two matrices of one type, in that type
+    (src/device/coopmat_intrinsics.jl:435-465). A GEMM starts its accumulator from
+    bias + residual with it: the bias loaded at stride 0, the residual at its own stride."""
+    assert a.dtype == b.dtype and a.shape == b.shape
+    return (a + b).astype(a.dtype)
+
+
+def coopmat_mul(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """coopmat_mul(a, b): component-wise OpFMul (src/device/coopmat_intrinsics.jl:402-433)."""
+    assert a.dtype == b.dtype and a.shape == b.shape
+    return (a * b).astype(a.dtype)
+
+
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 with round-to-nearest-even, as uint16 bits (the rounding OpFConvert
     specifies; src/compiler/spirv/coopmat.jl:783-822)."""

@@ -36,7 +36,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
     the C structs' sizes and field offsets, compiled from include/lvb.h by the host gcc."""
     structs = {"lvb_matrix_shape": lvb.lvb_matrix_shape, "lvb_device_caps": lvb.lvb_device_caps,
                "lvb_gemm_desc": lvb.lvb_gemm_desc, "lvb_gemm_plan": lvb.lvb_gemm_plan,
-               "lvb_attn_desc": lvb.lvb_attn_desc}
+               "lvb_attn_desc": lvb.lvb_attn_desc, "lvb_epilogue": lvb.lvb_epilogue}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "lvb.h"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
@@ -58,7 +58,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
 def test_library_needs_no_libcuda_at_load(lvb):
     out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
     assert "libcuda.so" not in out
-    assert lvb.abi_version() == 1
+    assert lvb.abi_version() == 2
 
 
 def test_static_caps_answer(lvb):
@@ -101,8 +101,8 @@ def _desc(lvb, **kw):
     (dict(c_type=5), 2, "no kernel for Float16 x Float16 -> Int32"),
     (dict(a_type=3, b_type=3, c_type=2), 2, "no kernel"),
     (dict(a_type=0, b_type=1), 2, "no kernel"),
-    (dict(a_rowmajor=0), 2, "row-major"),
-    (dict(b_rowmajor=1), 2, "row-major"),
+    (dict(a_rowmajor=0, lda=255), 1, "lda < M"),
+    (dict(b_rowmajor=1, ldb=100), 1, "ldb < N"),
     (dict(lda=100), 1, "lda < K"),
     (dict(ldb=255), 1, "ldb < K"),
     (dict(ldc=10), 1, "ldc < M"),
@@ -160,6 +160,51 @@ def test_plans(lvb):
     assert t.repack_a == 1 and t.repack_b == 1
     assert lvb.gemm_plan(64, 64, 72, lvb.I8, lvb.I32).repack_a == 1    # 72 bytes
     assert lvb.gemm_plan(64, 64, 80, lvb.I8, lvb.I32).repack_a == 0    # 80 = 5·16 bytes
+
+
+def test_plans_transposed_operands(lvb):
+    """MN-contiguous operands (Lava's transposing view): 16-bit ones are read MN-major in
+    place, 8-bit ones are copied K-major first."""
+    p = lvb.gemm_plan(4096, 4096, 4096, lvb.F16, lvb.F16, a_rowmajor=False, b_rowmajor=True)
+    assert (p.a_mnmajor, p.b_mnmajor, p.repack_a, p.repack_b) == (1, 1, 0, 0)
+    p = lvb.gemm_plan(4096, 4096, 4096, lvb.BF16, lvb.F32, b_rowmajor=True)
+    assert (p.a_mnmajor, p.b_mnmajor, p.repack_a, p.repack_b) == (0, 1, 0, 0)
+    q = lvb.gemm_plan(4096, 4096, 4096, lvb.I8, lvb.I32, a_rowmajor=False)
+    assert (q.a_mnmajor, q.repack_a, q.b_mnmajor, q.repack_b) == (0, 1, 0, 0)
+    # an MN-major leading dimension TMA cannot address (M=100 fp16 = 200 bytes) is copied
+    r = lvb.gemm_plan(100, 64, 64, lvb.F16, lvb.F32, a_rowmajor=False)
+    assert (r.a_mnmajor, r.repack_a) == (0, 1)
+
+
+def _epi(lvb, **kw):
+    e = lvb.lvb_epilogue()
+    for k, v in kw.items():
+        setattr(e, k, v)
+    return e
+
+
+@pytest.mark.parametrize("dkw,ekw,status,needle", [
+    (dict(), dict(activation=7), 1, "unknown activation"),
+    (dict(a_type=3, b_type=3, c_type=5), dict(activation=1), 2, "integer output"),
+    (dict(), dict(bias=256, bias_type=5), 2, "bias type"),
+    (dict(), dict(bias=256, bias_type=2, bias_axis=2), 1, "bias_axis"),
+    (dict(), dict(bias=258, bias_type=2), 1, "bias not aligned"),
+    (dict(), dict(residual=256, residual_type=3, ldr=256), 2, "residual type"),
+    (dict(), dict(residual=256, residual_type=0, ldr=100), 1, "ldr < M"),
+    (dict(c_rowmajor=1), dict(residual=256, residual_type=0, ldr=100), 1, "ldr < N"),
+    (dict(), dict(residual=257, residual_type=0, ldr=256), 1, "residual not aligned"),
+])
+def test_gemm_epilogue_validation(lvb, dkw, ekw, status, needle):
+    d = _desc(lvb, **dkw)
+    e = _epi(lvb, **ekw)
+    assert lvb.lib.lvb_gemm_ex_check(C.byref(d), C.byref(e)) == status
+    msg = lvb.lib.lvb_last_error().decode()
+    assert needle in msg and msg.startswith("lvb_gemm_ex: ")
+    # a valid epilogue passes; NULL is plain lvb_gemm
+    ok = _epi(lvb, bias=256, bias_type=lvb.F16, residual=512, residual_type=lvb.BF16, ldr=256,
+              activation=lvb.ACT_GELU_ERF)
+    assert lvb.lib.lvb_gemm_ex_check(C.byref(_desc(lvb)), C.byref(ok)) == 0
+    assert lvb.lib.lvb_gemm_ex_check(C.byref(_desc(lvb)), None) == 0
 
 
 

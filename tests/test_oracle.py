@@ -170,3 +170,48 @@ def test_golden_fixtures_reproduce():
             O = attention_ref(z["Q"].astype(np.float32), z["K"].astype(np.float32),
                               z["V"].astype(np.float32), bool(z["causal"]), float(z["scale"]))
             assert np.abs(O - z["O"]).max() < 1e-6, f.name
+
+
+def test_epilogue_init_is_stride0_bias_plus_residual():
+    """The fused GEMM's initial accumulator: bias read at stride 0 (per row = column-major
+    load, per column = row-major load) coopmat_add-ed to the residual, in Float32."""
+    from oracle.gemm import epilogue_init
+    b_row = np.array([1, 2, 3], dtype=np.float32)
+    b_col = np.array([10, 20], dtype=np.float32)
+    res = np.arange(6, dtype=np.float32).reshape(3, 2)
+    assert np.array_equal(epilogue_init(3, 2, b_row, "row"), [[1, 1], [2, 2], [3, 3]])
+    assert np.array_equal(epilogue_init(3, 2, b_col, "col"), [[10, 20]] * 3)
+    got = epilogue_init(3, 2, b_col, "col", res)
+    assert got.dtype == np.float32 and np.array_equal(got, res + b_col)
+    # Float32 addition: 2^24 + 1 rounds to 2^24, as the accumulator type does
+    big = epilogue_init(1, 1, np.array([2.0 ** 24], np.float32), "col", np.ones((1, 1), np.float32))
+    assert big[0, 0] == 2.0 ** 24
+
+
+def test_activation_known_values():
+    from oracle.gemm import ACTIVATIONS
+    x = np.array([-3.0, -1.0, 0.0, 1.0, 2.0])
+    assert np.array_equal(ACTIVATIONS["relu"](x), [0, 0, 0, 1, 2])
+    assert np.isnan(ACTIVATIONS["relu"](np.array([np.nan])))[0]       # NaN passes
+    # gelu(1) = Phi(1) = 0.841344746...; tanh form 0.841191990...
+    assert abs(ACTIVATIONS["gelu_erf"](np.array([1.0]))[0] - 0.8413447460685429) < 1e-15
+    assert abs(ACTIVATIONS["gelu"](np.array([1.0]))[0] - 0.8411919906082768) < 1e-15
+    assert abs(ACTIVATIONS["silu"](np.array([1.0]))[0] - 1.0 / (1.0 + np.exp(-1.0))) < 1e-15
+    assert ACTIVATIONS["silu"](np.array([-1000.0]))[0] == 0.0            # no overflow error
+
+
+def test_epilogue_ref_is_perelement_over_the_accumulator():
+    """gemm_epilogue_ref equals the vocabulary spelled out: accumulator init, muladd,
+    perelement(act), convert."""
+    from oracle.gemm import ACTIVATIONS, epilogue_init, gemm_epilogue_ref
+    rng = np.random.default_rng(0)
+    A = rng.uniform(-1, 1, (16, 32)).astype(np.float16)
+    B = rng.uniform(-1, 1, (32, 8)).astype(np.float16)
+    bias = rng.uniform(-1, 1, 8).astype(np.float32)
+    res = rng.uniform(-1, 1, (16, 8)).astype(np.float32)
+    acc = epilogue_init(16, 8, bias, "col", res).astype(np.float64)
+    acc = vocab.coopmat_muladd(A, B, acc)
+    f = lambda r, c, e: ACTIVATIONS["gelu"](np.array([e]))[0]
+    want = vocab.coopmat_convert(vocab.coopmat_perelement(f, acc), "Float16")
+    got = gemm_epilogue_ref(A, B, "Float16", bias, "col", res, "gelu")
+    assert np.array_equal(got, want)
