@@ -161,6 +161,27 @@ int make_tmap_2d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, u
   return LVB_OK;
 }
 
+int make_tmap_2d_sw(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
+                    uint64_t ld, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes,
+                    const char* op) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return fail(LVB_ERR_CUDA, op, "cuTensorMapEncodeTiled unavailable", "driver too old");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld * (uint64_t)esize};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = enc(tm, tma_type(esize), 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(LVB_ERR_UNSUPPORTED, op, "cuTensorMapEncodeTiled failed for a store map");
+  return LVB_OK;
+}
+
 int make_tmap_3d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
                  uint64_t outer, uint64_t ld_rows, uint64_t ld_outer, uint32_t box_inner,
                  uint32_t box_rows, const char* op) {
@@ -408,12 +429,30 @@ int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e) {
 }
 
 int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* out) {
+  const bool c_tma_ok = d && (d->ldc * dtype_size(d->c_type)) % 16 == 0;
+  return gemm_plan_c(d, sm_count, c_tma_ok, out);
+}
+
+}  // extern "C"
+namespace lvb {
+// c_tma_ok: C's base (when known) and leading dimension allow TMA stores.
+int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out) {
   int st = lvb_gemm_check(d);
   if (st) return st;
   if (!out) return fail(LVB_ERR_INVALID_ARG, "lvb_gemm", "plan is NULL");
   if (sm_count <= 0) sm_count = 148;
   std::memset(out, 0, sizeof *out);
-  out->swap_ab = d->c_rowmajor ? 1 : 0;
+  // Orientation: the kernel stores its accumulator rows (m) from TMEM lanes. When C can take
+  // TMA stores (leading dimension a 16-byte multiple), kernel-space n is C's contiguous
+  // dimension, so each thread's 32 columns are one contiguous run staged as 16-byte vectors;
+  // otherwise kernel-space m is, so a warp's direct stores of one column are contiguous.
+  // LVB_GEMM_STORE=direct forces the second (tuning).
+  static const bool env_direct = [] {
+    const char* s = std::getenv("LVB_GEMM_STORE");
+    return s && std::string(s) == "direct";
+  }();
+  const bool c_tma = c_tma_ok && !env_direct;
+  out->swap_ab = (d->c_rowmajor != 0) != c_tma ? 1 : 0;
   const int64_t kM = out->swap_ab ? d->N : d->M;
   const int64_t kN = out->swap_ab ? d->M : d->N;
   const int64_t tiles_m = (kM + 127) / 128;
@@ -465,6 +504,8 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
   out->b_mnmajor = b_mn && !out->repack_b;
   return LVB_OK;
 }
+}  // namespace lvb
+extern "C" {
 
 static int gemm_enqueue(const char* op, const lvb_gemm_desc* d, const lvb_epilogue* e,
                         const void* A, const void* B, void* C, void* stream) {
@@ -480,7 +521,9 @@ static int gemm_enqueue(const char* op, const lvb_gemm_desc* d, const lvb_epilog
   const bool epi = e && (e->bias || e->residual || e->activation != LVB_ACT_NONE);
   if (d->K == 0) return epi ? gemm_epilogue_only(d, e, C, s) : gemm_zero_fill(d, C, s);
   lvb_gemm_plan plan;
-  int st = lvb_gemm_plan_for(d, dev->sm_count, &plan);
+  const bool c_tma_ok =
+      (uintptr_t)C % 16 == 0 && (d->ldc * dtype_size(d->c_type)) % 16 == 0;
+  int st = gemm_plan_c(d, dev->sm_count, c_tma_ok, &plan);
   if (st) return st;
   if (((uintptr_t)A) % 16) plan.repack_a = 1, plan.a_mnmajor = 0;
   if (((uintptr_t)B) % 16) plan.repack_b = 1, plan.b_mnmajor = 0;

@@ -27,6 +27,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -49,8 +50,10 @@ struct GemmParams {
   int group_m;            // row-tiles per raster group
   int l2_mode;            // 0: A and B evict_last, 1: A evict_last / B evict_first, 2: no hint
   int a_mn, b_mn;         // operand staged MN-major (16-bit types only): the transposed view
+  int d_nmajor;           // D[m*ldd + n] (n contiguous) instead of D[m + n*ldd]
+  int stage_out;          // 1 (with d_nmajor): interior 32×32 boxes written by TMA tensor stores
   void* D;
-  long long ldd;          // D[m + n*ldd]
+  long long ldd;
   // Fused epilogue (kernel space): D = act(acc + (bias + R)).
   int epi;                // any of the below present
   int act;                // lvb_activation
@@ -68,6 +71,11 @@ struct GemmParams {
 // rows, each one TMA box; consecutive chunks 8 KB apart (the descriptor's leading byte
 // offset), 8-row K groups 1 KB apart (its stride byte offset).
 constexpr int kMnChunkBytes = 64 * 128;
+
+// Output staging for TMA stores: per epilogue warp two 32×32 sub-tiles of up to 4-byte
+// elements.
+constexpr int kStoreBufBytes = 32 * 32 * 4;
+constexpr int kStoreBytes = 4 * 2 * kStoreBufBytes;
 
 __device__ __forceinline__ float to_f32(float v) { return v; }
 __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
@@ -163,7 +171,7 @@ struct GemmCfg {
   static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int kBarBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStoreBytes + kBarBytes + 1024;
 };
 
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& tm, int& tn) {
@@ -196,41 +204,63 @@ __device__ __forceinline__ void store_out(void* D, long long idx, uint32_t bits)
   }
 }
 
-// v[j] = act(acc[j] + init[j]) for the 32 columns, then the clamped stores: the arithmetic is
-// straight-line code over independent elements.
-template <int OUT, int ACT>
-__device__ __forceinline__ void store_epi32(const GemmParams& p, const uint32_t (&r)[32],
-                                            const float (&init)[32], int m, int n0, int nv) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT>(__uint_as_float(r[j]) + init[j]);
-#pragma unroll
-  for (int j = 0; j < 32; ++j)
-    if (j < nv) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, __float_as_uint(v[j]));
+// Output conversion: fp32 / int32 bits -> the bits stored (RNE for 16-bit outputs).
+template <int OUT>
+__device__ __forceinline__ uint32_t cvt_out(uint32_t bits) {
+  if constexpr (OUT == OUT_F32 || OUT == OUT_I32) {
+    return bits;
+  } else if constexpr (OUT == OUT_F16) {
+    return __half_as_ushort(__float2half_rn(__uint_as_float(bits)));
+  } else {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(bits)));
+  }
 }
 
-// Store 32 columns n0.. of row m (one tcgen05.ld worth), clamped to N, with or without the
-// fused epilogue. Lanes hold consecutive m, so every column is one coalesced warp store (and
-// every residual column one coalesced warp load).
-template <int OUT>
-__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int m,
-                                            int n0, float bias_m) {
-  if (p.epi) {
-    if constexpr (OUT != OUT_I32) {
-      const int nv = min(32, p.N - n0);
-      float init[32];
+// r[j] = act(acc[j] + init[j]) for the 32 columns: straight-line code over independent
+// elements.
+template <int ACT>
+__device__ __forceinline__ void act32(uint32_t (&r)[32], const float (&init)[32]) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) init[j] = bias_m;
-      if (p.bias && !p.bias_on_m) add_loaded32(p.bias_kind, p.bias, n0, 1, nv, init);
-      if (p.res) add_loaded32(p.res_kind, p.res, (long long)n0 * p.ldr + m, p.ldr, nv, init);
-      switch (p.act) {
-        case LVB_ACT_RELU: store_epi32<OUT, LVB_ACT_RELU>(p, r, init, m, n0, nv); break;
-        case LVB_ACT_GELU_TANH: store_epi32<OUT, LVB_ACT_GELU_TANH>(p, r, init, m, n0, nv); break;
-        case LVB_ACT_GELU_ERF: store_epi32<OUT, LVB_ACT_GELU_ERF>(p, r, init, m, n0, nv); break;
-        case LVB_ACT_SILU: store_epi32<OUT, LVB_ACT_SILU>(p, r, init, m, n0, nv); break;
-        default: store_epi32<OUT, LVB_ACT_NONE>(p, r, init, m, n0, nv); break;
-      }
+  for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(act_fn<ACT>(__uint_as_float(r[j]) + init[j]));
+}
+
+// The fused epilogue on one tcgen05.ld worth (32 columns n0.. of row m), in place. `nv`
+// columns are inside the matrix (0 for a row past M: nothing is loaded for it).
+template <int OUT>
+__device__ __forceinline__ void apply_epilogue(const GemmParams& p, uint32_t (&r)[32], int m,
+                                               int n0, int nv, float bias_m) {
+  if constexpr (OUT != OUT_I32) {
+    float init[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) init[j] = bias_m;
+    if (p.bias && !p.bias_on_m) add_loaded32(p.bias_kind, p.bias, n0, 1, nv, init);
+    if (p.res) {
+      if (p.d_nmajor)
+        add_loaded32(p.res_kind, p.res, (long long)m * p.ldr + n0, 1, nv, init);
+      else
+        add_loaded32(p.res_kind, p.res, (long long)n0 * p.ldr + m, p.ldr, nv, init);
     }
+    switch (p.act) {
+      case LVB_ACT_RELU: act32<LVB_ACT_RELU>(r, init); break;
+      case LVB_ACT_GELU_TANH: act32<LVB_ACT_GELU_TANH>(r, init); break;
+      case LVB_ACT_GELU_ERF: act32<LVB_ACT_GELU_ERF>(r, init); break;
+      case LVB_ACT_SILU: act32<LVB_ACT_SILU>(r, init); break;
+      default: act32<LVB_ACT_NONE>(r, init); break;
+    }
+  }
+}
+
+// Direct store of 32 columns n0.. of row m, clamped to N. With D m-contiguous, lanes hold
+// consecutive m and every column is one warp store of 32 consecutive elements; with D
+// n-contiguous (edge boxes only) each thread writes its own run of up to 32 elements.
+template <int OUT>
+__device__ __forceinline__ void store_direct(const GemmParams& p, const uint32_t (&r)[32], int m,
+                                             int n0) {
+  if (p.d_nmajor) {
+    const long long base = (long long)m * p.ldd + n0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.N) store_out<OUT>(p.D, base + j, r[j]);
     return;
   }
   if (n0 + 32 <= p.N) {
@@ -240,6 +270,95 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (n0 + j < p.N) store_out<OUT>(p.D, (long long)(n0 + j) * p.ldd + m, r[j]);
+  }
+}
+
+template <int OUT>
+__device__ __forceinline__ uint32_t pack_out2(uint32_t a, uint32_t b) {
+  if constexpr (OUT == OUT_F16) {
+    __half2 v = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(a), __uint_as_float(b));
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Staged store (D n-contiguous): the warp's 32 (m) × 32 (n) sub-tile goes to shared memory
+// as [m][n] — each lane's 32 values are one contiguous row of 64 (16-bit) or 128 (32-bit)
+// bytes, written as 16-byte vectors — and one TMA tensor store of the box {32 n, 32 m} at
+// (n0, m0w) writes it out. The rows are stored with the tensor map's swizzle (64B for 64-byte
+// rows: 16-byte chunk c of row r at c ^ ((r >> 1) & 3); 128B for 128-byte rows: c ^ (r & 7)),
+// so the 32 lanes' vector stores hit distinct banks. Only boxes wholly inside the matrix take
+// this path (the store's clipping at the innermost edge is not exact to the element: a
+// 333-row matrix inside a 400-row buffer had rows 333.. overwritten), edge boxes use the
+// predicated direct stores. Two buffers per warp: a buffer is rewritten only after the store
+// issued from it two chunks earlier has finished reading it.
+template <int OUT>
+__device__ __forceinline__ void store_staged(const CUtensorMap* tmD, const uint32_t (&r)[32],
+                                             uint32_t sbase, uint32_t& cnt, int m0w, int n0) {
+  const uint32_t lane = lane_id();
+  const uint32_t buf = sbase + (cnt & 1) * kStoreBufBytes;
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  if constexpr (OUT == OUT_F16 || OUT == OUT_BF16) {
+    const uint32_t row = buf + lane * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      st_shared_v4(row + ((c ^ ((lane >> 1) & 3)) << 4), pack_out2<OUT>(r[8 * c], r[8 * c + 1]),
+                   pack_out2<OUT>(r[8 * c + 2], r[8 * c + 3]),
+                   pack_out2<OUT>(r[8 * c + 4], r[8 * c + 5]),
+                   pack_out2<OUT>(r[8 * c + 6], r[8 * c + 7]));
+  } else {
+    const uint32_t row = buf + lane * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      st_shared_v4(row + ((c ^ (lane & 7)) << 4), r[4 * c], r[4 * c + 1], r[4 * c + 2],
+                   r[4 * c + 3]);
+  }
+  fence_proxy_async_smem();  // this thread's writes -> visible to the TMA (async proxy)
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmD, buf, n0, m0w);
+    bulk_commit_group();
+  }
+  ++cnt;
+}
+
+// Drains this warp's 32 TMEM lanes of one accumulator (NCH chunks of 32 columns): the
+// tcgen05.ld of chunk c+1 is in flight while chunk c goes through the epilogue and its
+// stores, so the TMEM round trip is hidden. `release` hands the accumulator back as soon as
+// every chunk is in registers.
+template <int OUT, int NCH, typename Release>
+__device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap* tmD,
+                                          uint32_t t_row, int m, int m0w, int n_base,
+                                          float bias_m, uint32_t s_out, uint32_t& n_staged,
+                                          Release release) {
+  static_assert(NCH % 2 == 0, "chunks are drained in pairs");
+  const bool m_ok = m < p.M;
+  uint32_t ra[32], rb[32];
+  auto handle = [&](uint32_t (&r)[32], int c) {
+    const int n0 = n_base + c * 32;
+    if (p.epi) apply_epilogue<OUT>(p, r, m, n0, m_ok ? min(32, p.N - n0) : 0, bias_m);
+    if (p.stage_out && m0w + 32 <= p.M && n0 + 32 <= p.N)
+      store_staged<OUT>(tmD, r, s_out, n_staged, m0w, n0);
+    else if (m_ok)
+      store_direct<OUT>(p, r, m, n0);
+    __syncwarp();  // tcgen05.ld / wait are .sync.aligned: reconverge after the stores
+  };
+  tmem_ld32(t_row, ra);
+  tmem_wait_ld(ra);
+#pragma unroll 1
+  for (int c = 0; c < NCH; c += 2) {
+    tmem_ld32(t_row + (c + 1) * 32, rb);
+    handle(ra, c);
+    tmem_wait_ld(rb);
+    if (c + 2 < NCH)
+      tmem_ld32(t_row + (c + 2) * 32, ra);
+    else
+      release();
+    handle(rb, c + 1);
+    if (c + 2 < NCH) tmem_wait_ld(ra);
   }
 }
 
@@ -254,7 +373,7 @@ __device__ __forceinline__ uint64_t stage_desc(uint32_t saddr, int mn_major) {
 template <int AB, int OUT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
@@ -270,7 +389,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * kAStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* sStore = smem + S * Cfg::kStageBytes;   // [4 epilogue warps][2][32×32 elements]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
   uint64_t* full = bars;            // [S]  TMA -> MMA
   uint64_t* empty = bars + S;       // [S]  MMA -> TMA
   uint64_t* tfull = bars + 2 * S;   // [2]  MMA -> epilogue
@@ -395,6 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue ----------------
     const int ew = warp - 4;             // TMEM lanes 32*ew .. 32*ew+31
     const int row = ew * 32 + lane;
+    const uint32_t s_out = smem_u32(sStore) + ew * 2 * kStoreBufBytes;
+    uint32_t n_staged = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
@@ -407,21 +529,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float bias_m =
           (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * BN;
-      uint32_t r[32];
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the predicated stores
-        tmem_ld32(t_row + c * 32, r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
-          bar_arrive(&tempty[acc]);  // accumulator fully read: hand it back
-        }
-        if (m_ok) store_chunk<OUT>(p, r, m, tn * BN + c * 32, bias_m);
-      }
+      drain_acc<OUT, BN / 32>(p, &tmD, t_row, m, tm * kBM + ew * 32, tn * BN, bias_m, s_out,
+                              n_staged, [&] {
+                                tc_fence_before();
+                                bar_arrive(&tempty[acc]);  // accumulator fully read
+                              });
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (p.stage_out && lane == 0) bulk_wait_group<0>();  // stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -443,12 +559,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairStages = 6;
 constexpr int kPairHalfBytes = 128 * kRowBytes;             // 16 KB: 128 rows x 128 B
 constexpr int kPairStageBytes = 2 * kPairHalfBytes;         // A half + B half
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 256 + 1024;
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + kStoreBytes + 256 + 1024;
 
 template <int AB, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   constexpr int S = kPairStages;
   constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
   constexpr int kElemsPerRow = kInt ? 128 : 64;
@@ -463,7 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* sA = smem;                        // [S][128 rows][128 B]
   uint8_t* sB = smem + S * kPairHalfBytes;   // [S][128 rows][128 B]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kPairStageBytes);
+  uint8_t* sStore = smem + S * kPairStageBytes;    // [4 epilogue warps][2][32×32 elements]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
   uint64_t* full = bars;            // [S]  leader: both CTAs' TMA bytes
   uint64_t* empty = bars + S;       // [S]  both: MMA done with the stage
   uint64_t* tfull = bars + 2 * S;   // [2]  both: accumulator ready
@@ -595,6 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
     const int ew = warp - 4;
     const int row = ew * 32 + lane;
+    const uint32_t s_out = smem_u32(sStore) + ew * 2 * kStoreBufBytes;
+    uint32_t n_staged = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = cluster_id; t < p.total_tiles; t += nclusters) {
@@ -602,27 +721,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(t, p, tm, tn);
       if (!wait_bar(&tfull[acc], acc_phase, g, 34, t)) break;
       tc_fence_after();
-      const int m = tm * 256 + 128 * (int)rank + row;
+      const int m0 = tm * 256 + 128 * (int)rank;
+      const int m = m0 + row;
       const bool m_ok = m < p.M;
       const float bias_m =
           (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * 256;
-      uint32_t r[32];
-#pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
+      drain_acc<OUT, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out, n_staged, [&] {
+        tc_fence_before();
         __syncwarp();
-        tmem_ld32(t_row + c * 32, r);
-        tmem_wait_ld();
-        if (c == 7) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) bar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
-        }
-        if (m_ok) store_chunk<OUT>(p, r, m, tn * 256 + c * 32, bias_m);
-      }
+        if (lane == 0) bar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      });
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (p.stage_out && lane == 0) bulk_wait_group<0>();  // stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -660,7 +773,8 @@ int out_kind_of(int dt) {
 }
 
 template <int AB, int OUT, int BN>
-int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int ctas,
+int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+             const GemmParams& p, int ctas,
              cudaStream_t stream, DeviceState* dev) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<AB, OUT, BN>;
@@ -669,7 +783,7 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, 
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
-  kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, td, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "kernel launch");
   return LVB_OK;
@@ -678,7 +792,8 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, 
 // Persistent pair kernel: one cluster of 2 per SM pair, capped by how many clusters of this
 // kernel can be resident at once (GPC boundaries can leave an SM without a partner).
 template <int AB, int OUT>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int clusters,
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                const GemmParams& p, int clusters,
                 cudaStream_t stream, DeviceState* dev) {
   auto kern = gemm_tc2_kernel<AB, OUT>;
   cudaError_t e =
@@ -711,19 +826,19 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
     clusters = std::min(clusters, resident[dv]);
   }
   cfg.gridDim = dim3(2 * std::max(1, clusters));
-  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cluster kernel launch");
   return LVB_OK;
 }
 
 template <int AB, int OUT>
-int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-              int ctas, cudaStream_t s, DeviceState* dev) {
-  if (bn == 512) return launch_pair<AB, OUT>(ta, tb, p, ctas / 2, s, dev);
+int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+              const GemmParams& p, int ctas, cudaStream_t s, DeviceState* dev) {
+  if (bn == 512) return launch_pair<AB, OUT>(ta, tb, td, p, ctas / 2, s, dev);
   switch (bn) {
-    case 256: return launch_t<AB, OUT, 256>(ta, tb, p, ctas, s, dev);
-    case 128: return launch_t<AB, OUT, 128>(ta, tb, p, ctas, s, dev);
-    case 64: return launch_t<AB, OUT, 64>(ta, tb, p, ctas, s, dev);
+    case 256: return launch_t<AB, OUT, 256>(ta, tb, td, p, ctas, s, dev);
+    case 128: return launch_t<AB, OUT, 128>(ta, tb, td, p, ctas, s, dev);
+    case 64: return launch_t<AB, OUT, 64>(ta, tb, td, p, ctas, s, dev);
   }
   return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "tile width not built");
 }
@@ -959,7 +1074,8 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
   lvb_gemm_plan plan;
-  st = lvb_gemm_plan_for(d, sms, &plan);
+  st = gemm_plan_c(d, sms,
+                   (uintptr_t)C % 16 == 0 && (d->ldc * dtype_size(d->c_type)) % 16 == 0, &plan);
   if (st) return st;
   if (((uintptr_t)A) % 16) plan.repack_a = 1;
   if (((uintptr_t)B) % 16) plan.repack_b = 1;
@@ -1082,10 +1198,27 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
              : make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
                             plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
   if (st) return st;
+  // Kernel-space D is n-contiguous when the plan oriented the product that way (C can take
+  // TMA stores); its interior 32×32 boxes then go out through TMA tensor stores with the
+  // row swizzle the epilogue writes (64B for 16-bit, 128B for 32-bit elements).
+  const int osize = dtype_size(d->c_type);
+  const int d_nmajor = (plan.swap_ab != 0) != (d->c_rowmajor != 0);
+  CUtensorMap td;
+  std::memset(&td, 0, sizeof td);
+  int stage_out = 0;
+  if (d_nmajor) {
+    if (make_tmap_2d_sw(&td, C, osize, (uint64_t)kN, (uint64_t)kM, (uint64_t)d->ldc, 32, 32,
+                        osize == 2 ? 64 : 128, "lvb_gemm") == LVB_OK)
+      stage_out = 1;
+    else
+      clear_error();   // direct stores in the same orientation: correct, slower
+  }
 
   GemmParams p;
   p.a_mn = ka_mn;
   p.b_mn = kb_mn;
+  p.d_nmajor = d_nmajor;
+  p.stage_out = stage_out;
   set_epilogue(p, epi, plan.swap_ab != 0);
   p.M = (int)kM;
   p.N = (int)kN;
@@ -1116,17 +1249,17 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   const int bn = plan.cta_pair ? 512 : plan.tile_n;   // 512: the CTA-pair kernel
   const int ctas = plan.ctas;
   if (ab == AB_F16) {
-    if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, p, ctas, stream, dev);
-    if (out == OUT_F16) return launch_bn<AB_F16, OUT_F16>(bn, ta, tb, p, ctas, stream, dev);
-    if (out == OUT_BF16) return launch_bn<AB_F16, OUT_BF16>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, td, p, ctas, stream, dev);
+    if (out == OUT_F16) return launch_bn<AB_F16, OUT_F16>(bn, ta, tb, td, p, ctas, stream, dev);
+    if (out == OUT_BF16) return launch_bn<AB_F16, OUT_BF16>(bn, ta, tb, td, p, ctas, stream, dev);
   } else if (ab == AB_BF16) {
-    if (out == OUT_F32) return launch_bn<AB_BF16, OUT_F32>(bn, ta, tb, p, ctas, stream, dev);
-    if (out == OUT_F16) return launch_bn<AB_BF16, OUT_F16>(bn, ta, tb, p, ctas, stream, dev);
-    if (out == OUT_BF16) return launch_bn<AB_BF16, OUT_BF16>(bn, ta, tb, p, ctas, stream, dev);
+    if (out == OUT_F32) return launch_bn<AB_BF16, OUT_F32>(bn, ta, tb, td, p, ctas, stream, dev);
+    if (out == OUT_F16) return launch_bn<AB_BF16, OUT_F16>(bn, ta, tb, td, p, ctas, stream, dev);
+    if (out == OUT_BF16) return launch_bn<AB_BF16, OUT_BF16>(bn, ta, tb, td, p, ctas, stream, dev);
   } else if (ab == AB_S8 && out == OUT_I32) {
-    return launch_bn<AB_S8, OUT_I32>(bn, ta, tb, p, ctas, stream, dev);
+    return launch_bn<AB_S8, OUT_I32>(bn, ta, tb, td, p, ctas, stream, dev);
   } else if (ab == AB_U8 && out == OUT_I32) {
-    return launch_bn<AB_U8, OUT_I32>(bn, ta, tb, p, ctas, stream, dev);
+    return launch_bn<AB_U8, OUT_I32>(bn, ta, tb, td, p, ctas, stream, dev);
   }
   return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "dtype combination not built");
 }

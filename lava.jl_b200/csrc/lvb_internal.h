@@ -43,6 +43,12 @@ EncodeTiledFn encode_tiled_fn();
 int make_tmap_2d(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
                  uint64_t ld, uint32_t box_inner, uint32_t box_rows, const char* op);
 
+// The same with a chosen swizzle (0, 32, 64 or 128 bytes; 0 = boxes stored row-major in
+// shared memory), for TMA stores.
+int make_tmap_2d_sw(CUtensorMap* tm, const void* base, int esize, uint64_t inner, uint64_t rows,
+                    uint64_t ld, uint32_t box_inner, uint32_t box_rows, int swizzle_bytes,
+                    const char* op);
+
 // Rank-n tiled map (n <= 5), 128-byte swizzle. dims/box innermost first; strides[i] is the
 // element stride of dimension i+1.
 int make_tmap_nd(CUtensorMap* tm, const void* base, int esize, int rank, const uint64_t* dims,
@@ -57,6 +63,10 @@ int dtype_size(int dt);
 const char* dtype_name(int dt);
 
 // ---- GEMM (gemm_sm100.cu) ----
+// lvb_gemm_plan_for with C's TMA-store capability known (its base and leading dimension):
+// it decides the orientation of the product in kernel space.
+int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out);
+
 // `epi` is NULL for a plain GEMM.
 int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
                 const void* B, void* C, const lvb_epilogue* epi, cudaStream_t stream,

@@ -144,7 +144,9 @@ def test_plans(lvb):
     # large problems: 256x256 tiles on CTA pairs (cta_group::2), 74 pairs on 148 SMs
     assert p.cta_pair == 1
     assert (p.tile_m, p.tile_n, p.tile_k, p.instr_m, p.instr_k) == (256, 256, 64, 256, 16)
-    assert p.tiles == 32 * 32 and p.ctas == 148 and p.swap_ab == 0
+    # column-major C that can take TMA stores: computed as Cᵀ = BᵀAᵀ so the kernel's
+    # n is C's contiguous dimension (each thread's columns are one contiguous run)
+    assert p.tiles == 32 * 32 and p.ctas == 148 and p.swap_ab == 1
     assert p.tmem_cols == 512 and p.smem_bytes <= 232448 and p.stages == 6
     q = lvb.gemm_plan(8192, 8192, 8192, lvb.I8, lvb.I32)
     assert q.tile_k == 128 and q.instr_k == 32
@@ -154,7 +156,11 @@ def test_plans(lvb):
     r = lvb.gemm_plan(512, 512, 512, lvb.F16, lvb.F32)
     assert r.tile_n == 64 and r.tiles == 32          # latency-bound size: more CTAs
     s = lvb.gemm_plan(1000, 300, 64, lvb.F16, lvb.F32, c_rowmajor=True)
-    assert s.swap_ab == 1 and s.repack_a == 0 and s.repack_b == 0
+    assert s.swap_ab == 0 and s.repack_a == 0 and s.repack_b == 0
+    # a C leading dimension TMA cannot store to (N = 301 fp16 = 602 bytes): the other
+    # orientation, so direct stores of one column by a warp are contiguous
+    u = lvb.gemm_plan(1000, 301, 64, lvb.F16, lvb.F16, c_rowmajor=True)
+    assert u.swap_ab == 1
     # a leading dimension TMA cannot address (K=70 fp16 = 140 bytes) is repacked, not refused
     t = lvb.gemm_plan(64, 64, 70, lvb.F16, lvb.F32)
     assert t.repack_a == 1 and t.repack_b == 1
