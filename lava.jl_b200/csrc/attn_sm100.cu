@@ -15,7 +15,7 @@
 //     touches shared memory;
 //   * warp 8 lane 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through a
 //     5-slot ring of 128-key blocks (128B swizzle, zero fill past seq_kv);
-//   * warp 9 lane 0 (MMA): per key block j the tensor core runs PV_0(j), QK_0(j+1),
+//   * warp 9 (MMA; the warp waits, an elected lane issues): per key block j the tensor core runs PV_0(j), QK_0(j+1),
 //     PV_1(j), QK_1(j+1): while one tile's softmax works, the other tile's two products
 //     run. MMAs of one thread execute in order, so QK_t(j+1) overwriting S_t/P_t after
 //     PV_t(j) read P_t is ordered, and the commit that announces S_t(j+1) also covers
@@ -181,8 +181,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
   } else if (warp == 9) {
-    if (lane == 0 && n_blocks > 0) {
-      // ---------------- MMA issuer ----------------
+    if (n_blocks > 0) {
+      // ---------------- MMA issuer: the whole warp waits, one elected lane issues --------
       const uint32_t q_base = smem_u32(sQ);
       const uint32_t r_base = smem_u32(sRing);
       auto issue_qk = [&](int t, int slot) {
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint32_t o = (kk >> 2) * kChunk + (kk & 3) * 32;
           const uint64_t ad = sdesc_sw128(q_base + t * Cfg::kTileBytes + o, 16, 1024);
           const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + o, 16, 1024);
-          mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
+          if (elect_one()) mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int t, int slot, bool acc) {
@@ -201,56 +201,57 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
           const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
                                           kChunk, 1024);
-          mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
-                     (acc || kk > 0) ? 1u : 0u);
+          if (elect_one())
+            mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
+                       (acc || kk > 0) ? 1u : 0u);
         }
       };
       auto n_tile = [&](int t) { return t ? n_tile1 : n_tile0; };
-      bool ok = wait_bar(q_full, 0, g, 12, 0) && wait_bar(&ring_full[0], 0, g, 13, 0);
+      bool ok = wait_bar_warp(q_full, 0, g, 12, 0) && wait_bar_warp(&ring_full[0], 0, g, 13, 0);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < 2; ++t) {
           if (n_tile(t) == 0) continue;
           issue_qk(t, 0);
-          mma_commit(&s_full[t]);
+          if (elect_one()) mma_commit(&s_full[t]);
         }
-        mma_commit(&ring_empty[0]);  // K_0 (item 0)
+        if (elect_one()) mma_commit(&ring_empty[0]);  // K_0 (item 0)
       }
       for (int j = 0; j < n_blocks && ok; ++j) {
         const int iv = 2 * j + 1;             // V_j
         const int ik = 2 * j + 2;             // K_{j+1}
         const bool next = j + 1 < n_blocks;
-        if (!wait_bar(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) break;
+        if (!wait_bar_warp(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) break;
         bool k_ready = false;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j < n_tile(t)) {
-            if (!wait_bar(&p_full[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
+            if (!wait_bar_warp(&p_full[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, iv % R, j > 0);
-            mma_commit(&pv_done[t]);
+            if (elect_one()) mma_commit(&pv_done[t]);
           }
           if (j + 1 < n_tile(t)) {
             if (!k_ready) {
-              if (!wait_bar(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
+              if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
                 ok = false;
                 break;
               }
               k_ready = true;
             }
             issue_qk(t, ik % R);
-            mma_commit(&s_full[t]);
+            if (elect_one()) mma_commit(&s_full[t]);
           }
         }
         if (!ok) break;
-        mma_commit(&ring_empty[iv % R]);           // V_j done (both tiles)
+        if (elect_one()) mma_commit(&ring_empty[iv % R]);           // V_j done (both tiles)
         if (next) {
           if (!k_ready) {  // no tile used K_{j+1}: still consume it in order
-            if (!wait_bar(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) break;
+            if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) break;
           }
-          mma_commit(&ring_empty[ik % R]);         // K_{j+1} done
+          if (elect_one()) mma_commit(&ring_empty[ik % R]);         // K_{j+1} done
         }
       }
-      mma_commit(drain);
+      if (elect_one()) mma_commit(drain);
       drain_wait_a(drain, 0, p.timeout_ns);
     }
   } else {

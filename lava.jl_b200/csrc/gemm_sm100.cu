@@ -470,8 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < S; ++s)
         if (filled_mask & (1u << s)) drain_wait(&full[s], last_phase[s], p.timeout_ns);
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: the warp waits, one elected lane issues ----------------
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -484,32 +484,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_step = p.a_mn ? (16 * 128) >> 4 : kDescStep;
     const uint32_t b_step = p.b_mn ? (16 * 128) >> 4 : kDescStep;
     for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-      if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 2, t)) { ok = false; break; }
+      if (!wait_bar_warp(&tempty[acc], acc_phase ^ 1, g, 2, t)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!wait_bar(&full[stage], phase, g, 3, t)) { ok = false; break; }
+        if (!wait_bar_warp(&full[stage], phase, g, 3, t)) { ok = false; break; }
         tc_fence_after();
         const uint64_t adesc = stage_desc(a_base + stage * kAStageBytes, p.a_mn);
         const uint64_t bdesc = stage_desc(b_base + stage * Cfg::kBStageBytes, p.b_mn);
 #pragma unroll
         for (int k = 0; k < kMmasPerStage; ++k) {
           const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-          if constexpr (kInt)
-            mma_i8_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
-          else
-            mma_f16_ss(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
+          if (elect_one()) {
+            if constexpr (kInt)
+              mma_i8_ss(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+            else
+              mma_f16_ss(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
+          }
         }
-        mma_commit(&empty[stage]);
+        if (elect_one()) mma_commit(&empty[stage]);
         if (++stage == S) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
-      mma_commit(&tfull[acc]);
+      if (elect_one()) mma_commit(&tfull[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    // Every MMA this thread issued has finished before TMEM is released.
-    mma_commit(drain);
+    // Every MMA this warp issued has finished before TMEM is released.
+    if (elect_one()) mma_commit(drain);
     drain_wait(drain, 0, p.timeout_ns);
   } else if (warp >= 4) {
     // ---------------- epilogue ----------------
@@ -665,8 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < S; ++s)
         if (filled_mask & (1u << s)) drain_wait(&full[s], last_phase[s], p.timeout_ns);
     }
-  } else if (warp == 1 && lane == 0 && leader) {
-    // ---------------- MMA issuer (even CTA of the pair) ----------------
+  } else if (warp == 1 && leader) {
+    // ---------------- MMA issuer (even CTA of the pair; one elected lane issues) --------
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -678,35 +680,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t a_step = p.a_mn ? (16 * 128) >> 4 : kDescStep;
     const uint32_t b_step = p.b_mn ? (16 * 128) >> 4 : kDescStep;
     for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
-      if (!wait_bar(&tempty[acc], acc_phase ^ 1, g, 32, t)) { ok = false; break; }
+      if (!wait_bar_warp(&tempty[acc], acc_phase ^ 1, g, 32, t)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * 256;
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!wait_bar(&full[stage], phase, g, 33, t)) { ok = false; break; }
+        if (!wait_bar_warp(&full[stage], phase, g, 33, t)) { ok = false; break; }
         tc_fence_after();
         const uint64_t adesc = stage_desc(a_base + stage * kPairHalfBytes, p.a_mn);
         const uint64_t bdesc = stage_desc(b_base + stage * kPairHalfBytes, p.b_mn);
 #pragma unroll
         for (int k = 0; k < kMmasPerStage; ++k) {
           const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-          if constexpr (kInt)
-            mma_i8_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
-          else
-            mma_f16_ss_pair(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
+          if (elect_one()) {
+            if constexpr (kInt)
+              mma_i8_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+            else
+              mma_f16_ss_pair(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
+          }
         }
         const uint32_t e = smem_u32(&empty[stage]);
-        mma_commit_pair(mapa_shared(e, 0));
-        mma_commit_pair(mapa_shared(e, 1));
+        if (elect_one()) {
+          mma_commit_pair(mapa_shared(e, 0));
+          mma_commit_pair(mapa_shared(e, 1));
+        }
         if (++stage == S) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
       const uint32_t f = smem_u32(&tfull[acc]);
-      mma_commit_pair(mapa_shared(f, 0));
-      mma_commit_pair(mapa_shared(f, 1));
+      if (elect_one()) {
+        mma_commit_pair(mapa_shared(f, 0));
+        mma_commit_pair(mapa_shared(f, 1));
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
-    mma_commit_pair(mapa_shared(smem_u32(drain), 0));
+    if (elect_one()) mma_commit_pair(mapa_shared(smem_u32(drain), 0));
     drain_wait(drain, 0, p.timeout_ns);
   } else if (warp >= 4) {
     // ---------------- epilogue (both CTAs, own TMEM rows) ----------------
