@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define LVB_ABI_VERSION 2
+#define LVB_ABI_VERSION 3
 
 typedef enum lvb_status {
   LVB_OK = 0,
@@ -136,6 +136,11 @@ typedef struct lvb_gemm_plan {
   int32_t cta_pair;                  /* 1: 256x256 tiles on CTA pairs (tcgen05 cta_group::2) */
   int32_t a_mnmajor, b_mnmajor;      /* operand read by the tensor core MN-major, in place (A
                                         column-major / B row-major, 16-bit types) */
+  int32_t gemv;                      /* 1: N == 1 or M == 1 — a matrix-vector product, streamed
+                                        by the HBM-bound kernel (dot4x8 for 8-bit types), not
+                                        the tensor core; the tile fields above are then 0 */
+  int32_t gemv_ksplit;               /* k split across CTAs for it (partial sums in a
+                                        stream-ordered workspace, added in a fixed order) */
 } lvb_gemm_plan;
 
 /* Validate a descriptor (host only). */
@@ -149,8 +154,12 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
  * tensor view, permutation (1,0) (src/device/tensor_intrinsics.jl:212-320) — is read
  * MN-major in place when its type is 16-bit. An operand whose base or leading dimension is
  * not a 16-byte multiple, or an 8-bit operand stored MN-contiguous, is first copied K-major
- * on the device into a stream-ordered workspace (cudaMallocAsync / cudaFreeAsync on
- * `stream`). */
+ * on the device into a stream-ordered workspace (allocated on `stream` from the library's
+ * per-device memory pool, which keeps up to 512 MiB of freed workspace for the next call,
+ * and freed on `stream`). With N == 1 or M == 1 the product is a matrix-vector product and runs on the
+ * HBM-bound kernel instead (any layout; 8-bit operands through dot4x8, Lava's
+ * src/vocabulary/vocabulary.jl:18-35); when its rows alone cannot fill the GPU, k is split
+ * across CTAs with partial sums in a stream-ordered workspace. */
 int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
 
 /* Fused epilogue: C = act(A·B + bias + R), computed in fp32 and converted once to C's type.

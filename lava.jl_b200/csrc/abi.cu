@@ -114,8 +114,28 @@ DeviceState* current_device_state(const char* op) {
     fail_cuda(e, op, "allocating the device status word");
     return nullptr;
   }
+  // The library's own stream-ordered pool for workspaces. It keeps up to 512 MiB of freed
+  // workspace instead of handing it back at every synchronisation (the default pool's
+  // behaviour), so a workspace of the same size on the next call costs no mapping; the
+  // process's default pool is left as it is.
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  if (cudaMemPoolCreate(&st->pool, &props) == cudaSuccess) {
+    uint64_t keep = 512ull << 20;
+    cudaMemPoolSetAttribute(st->pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  } else {
+    cudaGetLastError();
+    st->pool = nullptr;   // workspaces then come from the default pool
+  }
   g_devices[dev] = st;
   return st;
+}
+
+cudaError_t workspace_alloc(DeviceState* dev, void** ptr, size_t bytes, cudaStream_t stream) {
+  if (dev && dev->pool) return cudaMallocFromPoolAsync(ptr, bytes, dev->pool, stream);
+  return cudaMallocAsync(ptr, bytes, stream);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -442,6 +462,14 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   if (!out) return fail(LVB_ERR_INVALID_ARG, "lvb_gemm", "plan is NULL");
   if (sm_count <= 0) sm_count = 148;
   std::memset(out, 0, sizeof *out);
+  if (gemv_applies(d)) {
+    GemvPlan g;
+    gemv_plan(d, sm_count, &g);
+    out->gemv = 1;
+    out->gemv_ksplit = g.ksplit;
+    out->ctas = g.ctas;
+    return LVB_OK;
+  }
   // Orientation: the kernel stores its accumulator rows (m) from TMEM lanes. When C can take
   // TMA stores (leading dimension a 16-byte multiple), kernel-space n is C's contiguous
   // dimension, so each thread's 32 columns are one contiguous run staged as 16-byte vectors;
@@ -520,6 +548,7 @@ static int gemm_enqueue(const char* op, const lvb_gemm_desc* d, const lvb_epilog
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool epi = e && (e->bias || e->residual || e->activation != LVB_ACT_NONE);
   if (d->K == 0) return epi ? gemm_epilogue_only(d, e, C, s) : gemm_zero_fill(d, C, s);
+  if (gemv_applies(d)) return gemv_launch(d, epi ? e : nullptr, A, B, C, s, dev);
   lvb_gemm_plan plan;
   const bool c_tma_ok =
       (uintptr_t)C % 16 == 0 && (d->ldc * dtype_size(d->c_type)) % 16 == 0;

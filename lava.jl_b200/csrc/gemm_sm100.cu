@@ -31,6 +31,7 @@
 #include <mutex>
 #include <string>
 
+#include "epilogue.cuh"
 #include "lvb_internal.h"
 
 namespace lvb {
@@ -77,16 +78,6 @@ constexpr int kMnChunkBytes = 64 * 128;
 constexpr int kStoreBufBytes = 32 * 32 * 4;
 constexpr int kStoreBytes = 4 * 2 * kStoreBufBytes;
 
-__device__ __forceinline__ float to_f32(float v) { return v; }
-__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
-__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
-
-__device__ __forceinline__ float load_as_f32(const void* p, int kind, long long i) {
-  if (kind == LVB_F32) return reinterpret_cast<const float*>(p)[i];
-  if (kind == LVB_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
-  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
-}
-
 // out[j] += X[i0 + j*stride] for j < nv. The 32 loads form one basic block ahead of the
 // conversions, so their latencies overlap.
 template <typename T>
@@ -105,37 +96,6 @@ __device__ __forceinline__ void add_loaded32(int kind, const void* base, long lo
   if (kind == LVB_F32) add_loaded32<float>(base, i0, stride, nv, out);
   else if (kind == LVB_F16) add_loaded32<__half>(base, i0, stride, nv, out);
   else add_loaded32<__nv_bfloat16>(base, i0, stride, nv, out);
-}
-
-// The per-element function of the epilogue (coopmat_perelement with a fixed callback).
-// gelu-tanh 0.5x(1 + tanh(u)) and silu are evaluated as x·sigmoid(t) = x / (1 + e^-t)
-// (t = 2u and t = x): the same functions, with no cancellation for negative arguments
-// (1 + tanh(u) -> 0) and a limit of -0 where e^-t overflows. gelu-erf as 0.5x·erfc(-x/√2),
-// which equals 0.5x(1 + erf(x/√2)) without the same cancellation.
-template <int ACT>
-__device__ __forceinline__ float act_fn(float v) {
-  if constexpr (ACT == LVB_ACT_RELU) {
-    return v < 0.f ? 0.f : v;  // NaN passes through, as max(x, 0) does in Julia
-  } else if constexpr (ACT == LVB_ACT_GELU_TANH) {
-    const float t = 1.5957691216057308f * fmaf(0.044715f * v, v * v, v);  // 2·sqrt(2/pi)·(...)
-    return __fdividef(v, 1.f + __expf(-t));
-  } else if constexpr (ACT == LVB_ACT_GELU_ERF) {
-    return 0.5f * v * erfcf(-0.7071067811865476f * v);
-  } else if constexpr (ACT == LVB_ACT_SILU) {
-    return __fdividef(v, 1.f + __expf(-v));
-  } else {
-    return v;
-  }
-}
-
-__device__ __forceinline__ float act_any(int act, float v) {
-  switch (act) {
-    case LVB_ACT_RELU: return act_fn<LVB_ACT_RELU>(v);
-    case LVB_ACT_GELU_TANH: return act_fn<LVB_ACT_GELU_TANH>(v);
-    case LVB_ACT_GELU_ERF: return act_fn<LVB_ACT_GELU_ERF>(v);
-    case LVB_ACT_SILU: return act_fn<LVB_ACT_SILU>(v);
-  }
-  return v;
 }
 
 // acc + (bias + R), then the activation, for one element: the accumulator started from
@@ -990,7 +950,7 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
   const size_t bytes_a = plan.repack_a ? (size_t)d->M * kp * es : 0;
   const size_t bytes_b = plan.repack_b ? (size_t)d->N * kp * es : 0;
   void* ws = nullptr;
-  cudaError_t e = cudaMallocAsync(&ws, bytes_a + bytes_b, stream);
+  cudaError_t e = workspace_alloc(dev, &ws, bytes_a + bytes_b, stream);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "workspace cudaMallocAsync");
   lvb_gemm_desc d2 = *d;
   lvb_gemm_plan plan2 = plan;

@@ -24,11 +24,16 @@ struct DeviceState {
   int cc_major = 0, cc_minor = 0;
   size_t smem_optin = 0;
   DevStatus* status = nullptr;   // device status word (cudaMalloc'd once per device)
+  cudaMemPool_t pool = nullptr;  // stream-ordered pool for workspaces (keeps freed memory)
 };
 // Returns nullptr (and sets the error) when the current device is unusable.
 DeviceState* current_device_state(const char* op);
 
 uint64_t wait_timeout_ns();
+
+// Stream-ordered workspace from the device's pool; release it with cudaFreeAsync on the
+// same stream.
+cudaError_t workspace_alloc(DeviceState* dev, void** ptr, size_t bytes, cudaStream_t stream);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -74,6 +79,19 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
 // K == 0 with an epilogue: C = act(bias + R).
 int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
                        cudaStream_t stream);
+
+// ---- matrix-vector products (gemv_sm100.cu): lvb_gemm with N == 1 or M == 1 ----
+struct GemvPlan {
+  int32_t k_contiguous;     // the matrix runs along k (one warp per row) or along rows
+  int32_t ksplit;           // k split across CTAs (partial sums in a workspace) when > 1
+  int64_t kchunk;           // elements of k per split
+  int32_t ctas;             // CTAs along the rows
+  int64_t workspace_bytes;  // ksplit·rows·4 when ksplit > 1
+};
+bool gemv_applies(const lvb_gemm_desc* d);
+int gemv_plan(const lvb_gemm_desc* d, int sm_count, GemvPlan* out);
+int gemv_launch(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, const void* B,
+                void* C, cudaStream_t stream, DeviceState* dev);
 
 // ---- attention (attn_sm100.cu) ----
 int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,

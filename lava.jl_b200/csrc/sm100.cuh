@@ -470,6 +470,17 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 16-byte global load of data read once (a matrix streamed by a matrix-vector product):
+// through the non-coherent path, not kept in L1.
+template <typename T>
+__device__ __forceinline__ uint4 ldg_stream_v4(const T* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),

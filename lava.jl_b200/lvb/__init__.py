@@ -101,7 +101,8 @@ class lvb_gemm_plan(C.Structure):
                 ("ctas", C.c_int32), ("smem_bytes", C.c_int32), ("tmem_cols", C.c_int32),
                 ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32),
                 ("repack_a", C.c_int32), ("repack_b", C.c_int32), ("cta_pair", C.c_int32),
-                ("a_mnmajor", C.c_int32), ("b_mnmajor", C.c_int32)]
+                ("a_mnmajor", C.c_int32), ("b_mnmajor", C.c_int32), ("gemv", C.c_int32),
+                ("gemv_ksplit", C.c_int32)]
 
 
 class lvb_epilogue(C.Structure):

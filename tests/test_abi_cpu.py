@@ -58,7 +58,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
 def test_library_needs_no_libcuda_at_load(lvb):
     out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
     assert "libcuda.so" not in out
-    assert lvb.abi_version() == 2
+    assert lvb.abi_version() == 3
 
 
 def test_static_caps_answer(lvb):
@@ -250,3 +250,15 @@ def test_attention_validation(lvb):
 def test_status_strings(lvb):
     assert lvb.lib.lvb_status_string(4) == b"LVB_ERR_TIMEOUT"
     assert lvb.lib.lvb_set_wait_timeout_ms(0) == lvb.LVB_ERR_INVALID_ARG
+
+
+def test_plan_routes_vectors_to_gemv(lvb):
+    """N == 1 or M == 1: the matrix-vector kernel, with k split across CTAs when the rows
+    alone cannot fill the GPU."""
+    p = lvb.gemm_plan(8192, 1, 8192, lvb.I8, lvb.I32)
+    assert p.gemv == 1 and p.instr_m == 0 and p.gemv_ksplit == 1
+    p = lvb.gemm_plan(1, 8192, 8192, lvb.F16, lvb.F32)
+    assert p.gemv == 1
+    p = lvb.gemm_plan(64, 1, 1 << 20, lvb.F16, lvb.F32)      # few rows: k split across CTAs
+    assert p.gemv == 1 and p.gemv_ksplit > 1
+    assert lvb.gemm_plan(8192, 2, 8192, lvb.F16, lvb.F32).gemv == 0
