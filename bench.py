@@ -56,14 +56,40 @@ WORKLOADS = {
                      causal=True, seed=3, dtype="f16"),
     "attn_bf16": dict(kind="attn", cfg="C5-attn", B=8, Hq=64, Hkv=8, S=16384, D=128,
                       ab="BFloat16", causal=True, seed=4, dtype="bf16"),
+    # HBM-bound shapes (roofline in GB/s against the measured copy bandwidth):
+    # decoding one token per sequence against C5's KV cache (the cache resident on the GPU)
+    "attn_decode_bf16": dict(kind="attn", cfg="C5-decode", B=8, Hq=64, Hkv=8, S=16384, Sq=1,
+                             D=128, ab="BFloat16", causal=True, seed=4, dtype="bf16",
+                             bound="hbm", resident_kv=True),
+    # int8 matrix-vector product (dot4x8), A 16384x16384 row-major (268 MB)
+    "gemv_i8": dict(kind="gemm", cfg="dot4x8-GEMV", M=16384, N=1, K=16384, ab="Int8",
+                    out="Int32", seed=2, dtype="int8", bound="hbm"),
 }
 
 
 def work_units(w) -> float:
     if w["kind"] == "gemm":
         return 2.0 * w["M"] * w["N"] * w["K"]
-    f = 4.0 * w["B"] * w["Hq"] * w["S"] * w["S"] * w["D"]
-    return f / 2 if w["causal"] else f
+    Sq, S = w.get("Sq", w["S"]), w["S"]
+    if Sq == S:
+        f = 4.0 * w["B"] * w["Hq"] * S * S * w["D"]
+        return f / 2 if w["causal"] else f
+    # query i sees keys j <= i + (S - Sq): the exact count of visible (query, key) pairs
+    pairs = sum(min(S, i + S - Sq + 1) for i in range(Sq)) if w["causal"] else Sq * S
+    return 4.0 * w["B"] * w["Hq"] * pairs * w["D"]
+
+
+ESIZE = {"Float16": 2, "BFloat16": 2, "Float32": 4, "Int8": 1, "Int32": 4}
+
+
+def algo_bytes(w) -> float:
+    """Bytes the op must move at least once: its operands and its result."""
+    if w["kind"] == "gemm":
+        e, o = ESIZE[w["ab"]], ESIZE[w["out"]]
+        return (w["M"] * w["K"] + w["K"] * w["N"]) * e + w["M"] * w["N"] * o
+    Sq = w.get("Sq", w["S"])
+    e = ESIZE[w["ab"]]
+    return (2 * w["B"] * w["Hq"] * Sq + 2 * w["B"] * w["Hkv"] * w["S"]) * w["D"] * e
 
 
 def measured_peaks():
@@ -200,11 +226,12 @@ def cpu_step_factory(w, target_s: float):
     # attention: whole (b, h) units at full sequence length
     from oracle.attention import attention_blockwise
     S, D = w["S"], w["D"]
-    q = g.standard_normal((S, D), dtype=np.float32)
+    Sq = w.get("Sq", S)
+    q = g.standard_normal((Sq, D), dtype=np.float32)
     k = g.standard_normal((S, D), dtype=np.float32)
     v = g.standard_normal((S, D), dtype=np.float32)
     units = 1
-    per = 4.0 * S * S * D / (2 if w["causal"] else 1)
+    per = work_units(w) / (w["B"] * w["Hq"])
     t0 = time.perf_counter()
     attention_blockwise(q, k, v, w["causal"], D ** -0.5, block=512)
     dt = time.perf_counter() - t0
@@ -213,7 +240,7 @@ def cpu_step_factory(w, target_s: float):
     def step():
         for _ in range(units):
             attention_blockwise(q, k, v, w["causal"], D ** -0.5, block=512)
-    sample = (f"{units} of {w['B'] * w['Hq']} (batch, head) units at S={S}, D={D}, "
+    sample = (f"{units} of {w['B'] * w['Hq']} (batch, head) units at Sq={Sq}, Skv={S}, D={D}, "
               "blockwise float32 online softmax on host BLAS")
     return step, units * per, sample
 
@@ -267,8 +294,8 @@ def config_of(w, n, reference=False):
         f"B {'row' if w.get('b_rowmajor', False) else 'column'}-major, C row-major"
         + (f", fused epilogue {w['epilogue']}(A·B + bias[n] + R), bias/R {w['out']}"
            if w.get("epilogue") else "") if w["kind"] == "gemm" else
-        f"{w['ab']} flash-attention fwd B={w['B']} Hq={w['Hq']} Hkv={w['Hkv']} S={w['S']} "
-        f"D={w['D']} causal={w['causal']} per GPU")}
+        f"{w['ab']} attention fwd B={w['B']} Hq={w['Hq']} Hkv={w['Hkv']} "
+        f"Sq={w.get('Sq', w['S'])} Skv={w['S']} D={w['D']} causal={w['causal']} per GPU")}
     c["parallelism"] = (f"row-shard x{n} (independent shards, no collective)" if w["kind"] == "gemm"
                         else f"(batch, kv-head) shard x{n}") if n > 1 else "single GPU"
     c["l2"] = "inputs larger than L2 (126 MB): working set re-read every step from HBM"
@@ -327,13 +354,21 @@ def make_attn(torch, lvb, w, rank):
     gen = torch.Generator(device="cuda").manual_seed(w["seed"] * 1000 + rank)
     tdt = {"Float16": torch.float16, "BFloat16": torch.bfloat16}[w["ab"]]
     Bn, Hq, Hkv, S, D = w["B"], w["Hq"], w["Hkv"], w["S"], w["D"]
-    Q = torch.randn((Bn, Hq, S, D), generator=gen, device="cuda").to(tdt)
+    Sq = w.get("Sq", S)
+    Q = torch.randn((Bn, Hq, Sq, D), generator=gen, device="cuda").to(tdt)
     K = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(tdt)
     V = torch.randn((Bn, Hkv, S, D), generator=gen, device="cuda").to(tdt)
     O = torch.empty_like(Q)
 
     def step():
         lvb.attention(O, Q, K, V, causal=w["causal"])
+
+    if w.get("resident_kv"):
+        # decoding: the KV cache is the serving loop's state on the GPU; a step's inputs are
+        # the new query rows and its result the output rows
+        def compute(d_ins, d_outs, stream):
+            lvb.attention(d_outs[0], d_ins[0], K, V, causal=w["causal"], stream=stream)
+        return step, compute, [Q], [O]
 
     def compute(d_ins, d_outs, stream):
         lvb.attention(d_outs[0], d_ins[0], d_ins[1], d_ins[2], causal=w["causal"], stream=stream)
@@ -535,6 +570,12 @@ def run_gpu(args, w):
         peak, burst = peak * scale, burst * scale
         achieved = units / (ms_local * 1e-3) / 1e12
         traffic = profile_traffic(args.workload)
+        hbm = w.get("bound") == "hbm"
+        if hbm:
+            # memory-bound shape: algorithmic bytes per launch over the launch time, against
+            # the measured copy bandwidth
+            hbm_peak = peaks.get("hbm_gbs", 6650.0)
+            gbs = algo_bytes(w) / (ms_local * 1e-3) / 1e9
         line = {
             "impl": "lvb", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -542,19 +583,28 @@ def run_gpu(args, w):
             "dtype": w["dtype"], "data": "synthetic: seeded torch RNG, shapes/distributions of "
             f"BASELINE {w['cfg']}",
             "config": config_of(w, world),
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_kind": kind, "timed_region_s": timed_s,
-                         "frac_of_burst": achieved / burst,
-                         "peak_source": f"{src} bf16_tflops{'_sustained' if kind == 'sustained' else ''}"
-                                        " (MEASURED_PEAKS.json)" if src.startswith("measured")
-                                        else f"{src} (1.59 burst / 1.40 sustained PFLOP/s)"},
+            "roofline": ({"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                          "frac": gbs / hbm_peak, "traffic": traffic,
+                          "algorithmic_bytes": algo_bytes(w), "timed_region_s": timed_s,
+                          "tensor_frac_of_burst": achieved / burst,
+                          "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)"
+                                         if src.startswith("measured") else f"{src} (6.65 TB/s)"}
+                         if hbm else
+                         {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit,
+                          "frac": achieved / peak, "traffic": traffic,
+                          "peak_kind": kind, "timed_region_s": timed_s,
+                          "frac_of_burst": achieved / burst,
+                          "peak_source": f"{src} bf16_tflops{'_sustained' if kind == 'sustained' else ''}"
+                                         " (MEASURED_PEAKS.json)" if src.startswith("measured")
+                                         else f"{src} (1.59 burst / 1.40 sustained PFLOP/s)"}),
             "e2e": None if args.no_e2e else {"value": units * world / (e2e_ms * 1e-3) / 1e12, "unit": unit,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "steps": e2e_steps,
                     "path": "lvb Python binding -> liblvb C ABI; pinned host buffers; every "
                             "step: H2D of its inputs, the op, D2H of its output, on copy-in / "
-                            "compute / copy-out streams over two device buffer sets"},
+                            "compute / copy-out streams over two device buffer sets"
+                            + ("; the KV cache stays resident on the GPU (decoding state)"
+                               if w.get("resident_kv") else "")},
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": args.steps,
@@ -586,7 +636,8 @@ def main():
         # about 2 s of timed device work at the expected rate
         args.steps = {"gemm_f16": 2000, "gemm_f16_512": 2000, "gemm_i8": 3000,
                       "gemm_bf16": 250, "attn_f16": 2000, "attn_bf16": 40,
-                      "gemm_f16_fused": 2000, "gemm_f16_mn": 2000}[args.workload]
+                      "gemm_f16_fused": 2000, "gemm_f16_mn": 2000,
+                      "attn_decode_bf16": 10000, "gemv_i8": 20000}[args.workload]
         if args.impl == "reference":
             args.steps = 5
     args.warmup = max(args.warmup, 3)

@@ -20,7 +20,8 @@ REPO = HERE.parent
 CSRC = HERE / "csrc"
 LIBDIR = HERE / "lib"
 LIB = LIBDIR / "liblvb.so"
-SOURCES = ["abi.cu", "gemm_sm100.cu", "gemv_sm100.cu", "attn_sm100.cu", "selftest.cu"]
+SOURCES = ["abi.cu", "gemm_sm100.cu", "gemv_sm100.cu", "attn_sm100.cu", "attn_decode_sm100.cu",
+           "selftest.cu"]
 HEADERS = ["sm100.cuh", "epilogue.cuh", "lvb_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

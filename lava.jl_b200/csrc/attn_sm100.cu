@@ -484,6 +484,8 @@ int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? LVB_OK : fail_cuda(e, op, "empty-softmax launch");
   }
+  if (attn_decode_applies(d))
+    return attn_decode_launch(d, qs, ks, vs, os, Q, K, V, O, lse, stream, dev);
   const uint32_t rowsbox = 128;
   CUtensorMap tq, tk, tv;
   {

@@ -96,5 +96,12 @@ int gemv_launch(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, co
 // ---- attention (attn_sm100.cu) ----
 int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,
                 float* lse, cudaStream_t stream, DeviceState* dev);
+// Few query rows per KV head (group·seq_q <= 32, head_dim 128): the HBM-bound decoding kernel
+// (attn_decode_sm100.cu), split over the key range.
+bool attn_decode_applies(const lvb_attn_desc* d);
+void attn_decode_plan(const lvb_attn_desc* d, int sm_count, int* nsplit, int* bps, int* ctas);
+int attn_decode_launch(const lvb_attn_desc* d, const long long qs[3], const long long ks[3],
+                       const long long vs[3], const long long os[3], const void* Q, const void* K,
+                       const void* V, void* O, float* lse, cudaStream_t stream, DeviceState* dev);
 
 }  // namespace lvb
