@@ -452,6 +452,19 @@ def run_gpu(args, w):
 
     step, compute, ins, outs = (make_gemm if w["kind"] == "gemm" else make_attn)(torch, lvb, w, rank)
     units = work_units(w)
+    # kernel launches of this library per step, from the library's own plan for the call
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    dt_of = {"Float16": lvb.F16, "BFloat16": lvb.BF16, "Int8": lvb.I8, "Float32": lvb.F32,
+             "Int32": lvb.I32}
+    if w["kind"] == "gemm":
+        launches_per_step = lvb.gemm_plan(
+            w["M"], w["N"], w["K"], dt_of[w["ab"]], dt_of[w["out"]], c_rowmajor=True,
+            sm_count=sms, a_rowmajor=w.get("a_rowmajor", True),
+            b_rowmajor=w.get("b_rowmajor", False)).launches
+    else:
+        launches_per_step = lvb.attention_plan(
+            w["B"], w["Hq"], w["Hkv"], w.get("Sq", w["S"]), w["S"], w["D"], dt_of[w["ab"]],
+            w["causal"], sm_count=sms).launches
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -563,6 +576,7 @@ def run_gpu(args, w):
         peak = peaks.get("bf16_tflops_sustained", burst) if kind == "sustained" else burst
         unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
         scale = 1.0
+        hbm_src = src
         if w["ab"] == "Int8":
             # no measured int8 peak: dense int8 is twice dense bf16 on this part
             scale = 2.0
@@ -587,8 +601,8 @@ def run_gpu(args, w):
                           "frac": gbs / hbm_peak, "traffic": traffic,
                           "algorithmic_bytes": algo_bytes(w), "timed_region_s": timed_s,
                           "tensor_frac_of_burst": achieved / burst,
-                          "peak_source": f"{src} hbm_gbs (MEASURED_PEAKS.json)"
-                                         if src.startswith("measured") else f"{src} (6.65 TB/s)"}
+                          "peak_source": f"{hbm_src} hbm_gbs (MEASURED_PEAKS.json)"
+                                         if hbm_src.startswith("measured") else f"{hbm_src} (6.65 TB/s)"}
                          if hbm else
                          {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": unit,
                           "frac": achieved / peak, "traffic": traffic,
@@ -607,7 +621,7 @@ def run_gpu(args, w):
                                if w.get("resident_kv") else "")},
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * launches_per_step,
             "allgather": allgather,
         }
         if unfused:

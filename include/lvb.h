@@ -141,6 +141,8 @@ typedef struct lvb_gemm_plan {
                                         the tensor core; the tile fields above are then 0 */
   int32_t gemv_ksplit;               /* k split across CTAs for it (partial sums in a
                                         stream-ordered workspace, added in a fixed order) */
+  int32_t launches;                  /* kernel launches per call, operand copies and the
+                                        split sums included (0 for an empty C) */
 } lvb_gemm_plan;
 
 /* Validate a descriptor (host only). */
@@ -241,6 +243,23 @@ typedef struct lvb_attn_desc {
 } lvb_attn_desc;
 
 int lvb_attention_check(const lvb_attn_desc* d);
+
+/* Which kernel lvb_attention_fwd runs for a descriptor (host only, no GPU). */
+typedef enum lvb_attn_kernel {
+  LVB_ATTN_FLASH = 0,   /* two 128-row query tiles per CTA, keys streamed in 128-key blocks */
+  LVB_ATTN_DECODE = 1,  /* few query rows per KV head (group·seq_q <= 32, head_dim 128): the
+                           KV cache streamed once, split over the keys, splits merged after */
+  LVB_ATTN_EMPTY = 2    /* seq_kv == 0: O = 0, lse = -inf */
+} lvb_attn_kernel;
+
+typedef struct lvb_attn_plan {
+  int32_t kernel;     /* lvb_attn_kernel */
+  int32_t splits;     /* key-range splits per (batch, KV head) (LVB_ATTN_DECODE), else 1 */
+  int32_t ctas;       /* CTAs of the main kernel */
+  int32_t launches;   /* kernel launches per call (0 when there is no output) */
+} lvb_attn_plan;
+
+int lvb_attention_plan_for(const lvb_attn_desc* d, int32_t sm_count, lvb_attn_plan* out);
 /* Enqueue the forward pass. `lse` (nullable) receives the fp32 natural-log row
  * log-sum-exp of scale·QKᵀ, laid out [batch][heads_q][seq_q]. */
 int lvb_attention_fwd(const lvb_attn_desc* d, const void* Q, const void* K, const void* V,

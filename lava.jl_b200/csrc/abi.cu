@@ -462,12 +462,14 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   if (!out) return fail(LVB_ERR_INVALID_ARG, "lvb_gemm", "plan is NULL");
   if (sm_count <= 0) sm_count = 148;
   std::memset(out, 0, sizeof *out);
+  if (d->M == 0 || d->N == 0) return LVB_OK;   // nothing to launch
   if (gemv_applies(d)) {
     GemvPlan g;
     gemv_plan(d, sm_count, &g);
     out->gemv = 1;
     out->gemv_ksplit = g.ksplit;
     out->ctas = g.ctas;
+    out->launches = g.ksplit > 1 ? 2 : 1;
     return LVB_OK;
   }
   // Orientation: the kernel stores its accumulator rows (m) from TMEM lanes. When C can take
@@ -530,6 +532,7 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   out->repack_b = (d->ldb * es) % 16 != 0 || (b_mn && es == 1);
   out->a_mnmajor = a_mn && !out->repack_a;
   out->b_mnmajor = b_mn && !out->repack_b;
+  out->launches = d->K == 0 ? 1 : 1 + out->repack_a + out->repack_b;
   return LVB_OK;
 }
 }  // namespace lvb
@@ -600,6 +603,34 @@ int lvb_attention_check(const lvb_attn_desc* d) {
     if ((s[0] * 2) % 16 || (s[1] * 2) % 16 || (s[2] * 2) % 16)
       return fail(LVB_ERR_UNSUPPORTED, op, "strides must be multiples of 16 bytes");
   }
+  return LVB_OK;
+}
+
+int lvb_attention_plan_for(const lvb_attn_desc* d, int32_t sm_count, lvb_attn_plan* out) {
+  int st = lvb_attention_check(d);
+  if (st) return st;
+  if (!out) return fail(LVB_ERR_INVALID_ARG, "lvb_attention_fwd", "plan is NULL");
+  if (sm_count <= 0) sm_count = 148;
+  std::memset(out, 0, sizeof *out);
+  out->splits = 1;
+  if (d->batch == 0 || d->heads_q == 0 || d->seq_q == 0) return LVB_OK;
+  if (d->seq_kv == 0) {
+    out->kernel = LVB_ATTN_EMPTY;
+    out->launches = 1;
+    return LVB_OK;
+  }
+  if (attn_decode_applies(d)) {
+    int ns = 1, bps = 1, ctas = 1;
+    attn_decode_plan(d, sm_count, &ns, &bps, &ctas);
+    out->kernel = LVB_ATTN_DECODE;
+    out->splits = ns;
+    out->ctas = ctas;
+    out->launches = ns > 1 ? 2 : 1;
+    return LVB_OK;
+  }
+  out->kernel = LVB_ATTN_FLASH;
+  out->ctas = (int32_t)(((d->seq_q + 255) / 256) * d->batch * d->heads_q);
+  out->launches = 1;
   return LVB_OK;
 }
 

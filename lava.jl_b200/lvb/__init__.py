@@ -47,7 +47,7 @@ EXPORTS = [
     "lvb_caps_sm100", "lvb_caps", "lvb_matrix_shapes", "lvb_bestshape",
     "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm", "lvb_gemm_noalloc",
     "lvb_gemm_ex_check", "lvb_gemm_ex",
-    "lvb_attention_check", "lvb_attention_fwd",
+    "lvb_attention_check", "lvb_attention_plan_for", "lvb_attention_fwd",
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
     "lvb_stream_create", "lvb_stream_destroy", "lvb_stream_synchronize",
@@ -102,7 +102,12 @@ class lvb_gemm_plan(C.Structure):
                 ("instr_m", C.c_int32), ("instr_n", C.c_int32), ("instr_k", C.c_int32),
                 ("repack_a", C.c_int32), ("repack_b", C.c_int32), ("cta_pair", C.c_int32),
                 ("a_mnmajor", C.c_int32), ("b_mnmajor", C.c_int32), ("gemv", C.c_int32),
-                ("gemv_ksplit", C.c_int32)]
+                ("gemv_ksplit", C.c_int32), ("launches", C.c_int32)]
+
+
+class lvb_attn_plan(C.Structure):
+    _fields_ = [("kernel", C.c_int32), ("splits", C.c_int32), ("ctas", C.c_int32),
+                ("launches", C.c_int32)]
 
 
 class lvb_epilogue(C.Structure):
@@ -138,6 +143,7 @@ def _load() -> C.CDLL:
         "lvb_gemm_ex": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue), P, P, P, P], C.c_int),
         "lvb_attention_check": ([C.POINTER(lvb_attn_desc)], C.c_int),
         "lvb_attention_fwd": ([C.POINTER(lvb_attn_desc), P, P, P, P, P, P], C.c_int),
+        "lvb_attention_plan_for": ([C.POINTER(lvb_attn_desc), C.c_int32, C.POINTER(lvb_attn_plan)], C.c_int),
         "lvb_abi_version": ([], C.c_int),
         "lvb_last_error": ([], C.c_char_p),
         "lvb_status_string": ([C.c_int], C.c_char_p),
@@ -432,6 +438,21 @@ def attention(O, Q, K, V, causal=True, scale=None, lse=None, stream=None):
                                 O.data_ptr(), lse.data_ptr() if lse is not None else None,
                                 _stream_ptr(stream)))
     return O
+
+
+ATTN_FLASH, ATTN_DECODE, ATTN_EMPTY = 0, 1, 2
+
+
+def attention_plan(B, Hq, Hkv, Sq, Skv, D=128, dtype=BF16, causal=True,
+                   sm_count=148) -> lvb_attn_plan:
+    """The kernel lvb_attention_fwd picks for these extents (host only, no GPU)."""
+    d = lvb_attn_desc()
+    d.dtype, d.causal = dtype, int(bool(causal))
+    d.batch, d.heads_q, d.heads_kv, d.seq_q, d.seq_kv, d.head_dim = B, Hq, Hkv, Sq, Skv, D
+    d.scale = float(D) ** -0.5
+    p = lvb_attn_plan()
+    check(lib.lvb_attention_plan_for(C.byref(d), sm_count, C.byref(p)))
+    return p
 
 
 def attention_available() -> bool:

@@ -36,7 +36,8 @@ def test_struct_layouts_match_header(lvb, tmp_path):
     the C structs' sizes and field offsets, compiled from include/lvb.h by the host gcc."""
     structs = {"lvb_matrix_shape": lvb.lvb_matrix_shape, "lvb_device_caps": lvb.lvb_device_caps,
                "lvb_gemm_desc": lvb.lvb_gemm_desc, "lvb_gemm_plan": lvb.lvb_gemm_plan,
-               "lvb_attn_desc": lvb.lvb_attn_desc, "lvb_epilogue": lvb.lvb_epilogue}
+               "lvb_attn_desc": lvb.lvb_attn_desc, "lvb_epilogue": lvb.lvb_epilogue,
+               "lvb_attn_plan": lvb.lvb_attn_plan}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "lvb.h"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
@@ -262,3 +263,24 @@ def test_plan_routes_vectors_to_gemv(lvb):
     p = lvb.gemm_plan(64, 1, 1 << 20, lvb.F16, lvb.F32)      # few rows: k split across CTAs
     assert p.gemv == 1 and p.gemv_ksplit > 1
     assert lvb.gemm_plan(8192, 2, 8192, lvb.F16, lvb.F32).gemv == 0
+    assert lvb.gemm_plan(8192, 1, 8192, lvb.I8, lvb.I32).launches == 1
+    assert lvb.gemm_plan(64, 1, 1 << 20, lvb.F16, lvb.F32).launches == 2     # + the split sums
+    assert lvb.gemm_plan(8192, 8192, 8192, lvb.F16, lvb.F16).launches == 1
+    assert lvb.gemm_plan(64, 64, 72, lvb.I8, lvb.I32).launches == 3          # + repacks of A and B
+    assert lvb.gemm_plan(0, 64, 72, lvb.I8, lvb.I32).launches == 0
+
+
+def test_attention_plans(lvb):
+    """Few query rows per KV head take the decoding kernel, split over a long cache; long
+    query sequences the flash kernel; an empty key sequence the fill kernel."""
+    p = lvb.attention_plan(8, 64, 8, 1, 16384)              # C5's cache, one new token
+    assert p.kernel == lvb.ATTN_DECODE and p.splits > 1 and p.launches == 2 and p.ctas == 148
+    p = lvb.attention_plan(64, 32, 32, 1, 2048)              # many heads: no split needed
+    assert p.kernel == lvb.ATTN_DECODE and p.splits == 1 and p.launches == 1
+    assert lvb.attention_plan(1, 32, 1, 1, 300).kernel == lvb.ATTN_DECODE   # 32 rows
+    assert lvb.attention_plan(1, 64, 1, 1, 300).kernel == lvb.ATTN_FLASH    # 64 rows
+    assert lvb.attention_plan(1, 8, 8, 1, 300, D=64).kernel == lvb.ATTN_FLASH
+    p = lvb.attention_plan(4, 32, 32, 4096, 4096, dtype=lvb.F16)
+    assert p.kernel == lvb.ATTN_FLASH and p.ctas == 16 * 128 and p.launches == 1
+    assert lvb.attention_plan(2, 4, 4, 10, 0).kernel == lvb.ATTN_EMPTY
+    assert lvb.attention_plan(0, 4, 4, 10, 10).launches == 0
