@@ -1066,6 +1066,14 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   if (d->K == 0) return gemm_zero_fill(d, C, s);
 
   DeviceState local;  // no allocation: the status word is the scratch head
+  if (gemv_applies(d)) {
+    // A matrix-vector product: the streaming kernel without its k split (whose partial sums
+    // would need a workspace), so nothing is allocated.
+    local.device = device;
+    local.sm_count = sms;
+    local.status = status;
+    return gemv_launch(d, nullptr, A, B, C, s, &local, /*allow_workspace=*/false);
+  }
   local.device = device;
   local.sm_count = sms;
   local.status = status;

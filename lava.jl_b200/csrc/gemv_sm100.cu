@@ -363,10 +363,15 @@ int gemv_plan(const lvb_gemm_desc* d, int sm_count, GemvPlan* out) {
 }
 
 int gemv_launch(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, const void* B,
-                void* C, cudaStream_t stream, DeviceState* dev) {
+                void* C, cudaStream_t stream, DeviceState* dev, bool allow_workspace) {
   const int es = dtype_size(d->a_type);
   GemvPlan plan;
   gemv_plan(d, dev->sm_count, &plan);
+  if (!allow_workspace) {
+    plan.ksplit = 1;
+    plan.kchunk = d->K;
+    plan.workspace_bytes = 0;
+  }
   const bool n1 = d->N == 1;
   GemvParams p = {};
   if (n1) {

@@ -90,8 +90,9 @@ struct GemvPlan {
 };
 bool gemv_applies(const lvb_gemm_desc* d);
 int gemv_plan(const lvb_gemm_desc* d, int sm_count, GemvPlan* out);
+// allow_workspace = false: never split k (no partial-sum workspace is allocated).
 int gemv_launch(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, const void* B,
-                void* C, cudaStream_t stream, DeviceState* dev);
+                void* C, cudaStream_t stream, DeviceState* dev, bool allow_workspace = true);
 
 // ---- attention (attn_sm100.cu) ----
 int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void* V, void* O,
