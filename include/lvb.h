@@ -246,9 +246,11 @@ int lvb_attention_check(const lvb_attn_desc* d);
 
 /* Which kernel lvb_attention_fwd runs for a descriptor (host only, no GPU). */
 typedef enum lvb_attn_kernel {
-  LVB_ATTN_FLASH = 0,   /* two 128-row query tiles per CTA, keys streamed in 128-key blocks */
+  LVB_ATTN_FLASH = 0,   /* persistent CTAs, two 128-row query tiles per work item, keys
+                           streamed in 128-key blocks */
   LVB_ATTN_DECODE = 1,  /* few query rows per KV head (group·seq_q <= 32, head_dim 128): the
-                           KV cache streamed once, split over the keys, splits merged after */
+                           KV cache streamed once, split over the keys; the CTA that finishes
+                           a (batch, KV head)'s last split merges them */
   LVB_ATTN_EMPTY = 2    /* seq_kv == 0: O = 0, lse = -inf */
 } lvb_attn_kernel;
 

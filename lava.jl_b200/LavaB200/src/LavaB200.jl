@@ -239,6 +239,11 @@ matrix in C's layout (may be `C` itself); `activation` one of `:none, :relu, :ge
 (tanh form), `:gelu_erf, :silu` — the accumulator initialised with `coopmat_add(bias,
 residual)` and finished with `coopmat_perelement` (src/device/coopmat_intrinsics.jl:
 435-447,551-593). Floating-point outputs only.
+
+A device vector as `B` and `C` (N == 1), or a 1×K `A` (M == 1), is a matrix-vector product:
+it runs on the library's HBM-bound streaming kernel — `dot4x8` for Int8/UInt8 operands
+(src/vocabulary/vocabulary.jl:18-35), fp32 multiply-adds for Float16/BFloat16 — with the
+same results and epilogue.
 """
 function gemm!(C, A, B; bias = nothing, bias_axis::Symbol = :row, residual = nothing,
                activation::Symbol = :none, stream::Ptr{Cvoid} = C_NULL)
@@ -283,6 +288,8 @@ end
 
 Flash-attention forward. Q, O: `(E, Lq, Hq, B)`; K, V: `(E, Lk, Hkv, B)` (column-major,
 dense); `lse` (optional, Float32 `(Lq, Hq, B)`) receives the natural-log row log-sum-exp.
+With at most 32 query rows per KV head (`Lq · Hq/Hkv <= 32`, E = 128) — decoding against a
+KV cache — the library streams the cache once, split over the keys, instead.
 """
 function attention!(O, Q, K, V; causal::Bool = true, scale::Real = inv(sqrt(size(Q, 1))),
                     lse = nothing, stream::Ptr{Cvoid} = C_NULL)

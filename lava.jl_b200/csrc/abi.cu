@@ -625,11 +625,12 @@ int lvb_attention_plan_for(const lvb_attn_desc* d, int32_t sm_count, lvb_attn_pl
     out->kernel = LVB_ATTN_DECODE;
     out->splits = ns;
     out->ctas = ctas;
-    out->launches = ns > 1 ? 2 : 1;
+    out->launches = 1;   // the last split of each (batch, KV head) merges in the same kernel
     return LVB_OK;
   }
   out->kernel = LVB_ATTN_FLASH;
-  out->ctas = (int32_t)(((d->seq_q + 255) / 256) * d->batch * d->heads_q);
+  const long long items = ((d->seq_q + 255) / 256) * d->batch * d->heads_q;
+  out->ctas = (int32_t)std::min<long long>(items, sm_count);   // persistent
   out->launches = 1;
   return LVB_OK;
 }

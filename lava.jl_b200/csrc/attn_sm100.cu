@@ -25,8 +25,10 @@
 //     domain with the scale folded in; the O rescale is lazy (only when the running max
 //     grows by more than 2^8, which keeps every p <= 256) and done in TMEM by the same
 //     warp;
-//   * grid (query-tile pairs, batch·heads), heaviest causal pair first inside a head; the
-//     pairs of one head run side by side and share its K/V blocks in L2.
+//   * persistent: one CTA per SM takes (head, query-tile pair) items from a global counter,
+//     head by head and the heaviest causal pair of a head first, so the items in flight
+//     share a few heads' K/V blocks in L2; the TMA warp publishes the next item through a
+//     shared-memory queue and loads its Q and first K/V blocks while the current item ends.
 #include <algorithm>
 #include <cmath>
 
@@ -39,6 +41,8 @@ constexpr int kChunk = 128 * 128;       // bytes of one 128-row x 64-element swi
 
 struct AttnParams {
   int B, Hq, Hkv, Sq, Skv, group, num_pairs, causal;
+  int total_items;             // num_pairs · B · Hq work items
+  int* work_counter;           // zero at launch; items are taken from it in order
   float scale_log2;
   void* O;
   long long o_sb, o_sh, o_ss;  // element strides of batch, head, seq
@@ -52,7 +56,7 @@ struct AttnCfg {
   static constexpr int kTileBytes = 128 * D * 2;  // Q tile or K/V block
   static constexpr int kQBytes = 2 * kTileBytes;
   static constexpr int kRing = D == 128 ? 5 : 8;
-  static constexpr int kSmem = kQBytes + kRing * kTileBytes + 256 + 1024;
+  static constexpr int kSmem = kQBytes + kRing * kTileBytes + 512 + 1024;   // + barriers
 };
 
 __device__ __forceinline__ void drain_wait_a(uint64_t* bar, uint32_t parity, uint64_t timeout_ns) {
@@ -74,9 +78,46 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
+// Geometry of one work item = (batch·head, pair of 128-row query tiles). Items are numbered
+// head by head, the heaviest causal pair of a head first, and handed out in that order, so
+// the CTAs running at any moment work on a few heads and share their K/V blocks in L2.
+struct AttnItem {
+  int b, h, hk, q0, n_tile0, n_tile1, n_blocks;
+};
+
+__device__ __forceinline__ AttnItem attn_item(int item, const AttnParams& p) {
+  AttnItem it;
+  const int bh = item / p.num_pairs;
+  const int pair = p.num_pairs - 1 - (item - bh * p.num_pairs);
+  it.b = bh / p.Hq;
+  it.h = bh - it.b * p.Hq;
+  it.hk = it.h / p.group;
+  it.q0 = pair * 256;
+  const int off = p.Skv - p.Sq;  // query q sees keys <= q + off
+  const int kv_blocks = (p.Skv + 127) / 128;
+  // Key blocks per query tile: under the causal mask tile 0 stops one block earlier than
+  // tile 1 whenever its last row's keys end before tile 1's; n_blocks = max over the tiles.
+  it.n_tile0 = kv_blocks;
+  it.n_tile1 = kv_blocks;
+  if (p.causal) {
+    const int last0 = min(it.q0 + 127, p.Sq - 1) + off;
+    const int last1 = min(it.q0 + 255, p.Sq - 1) + off;
+    it.n_tile0 = last0 < 0 ? 0 : min(kv_blocks, last0 / 128 + 1);
+    it.n_tile1 = last1 < 0 ? 0 : min(kv_blocks, last1 / 128 + 1);
+  }
+  it.n_blocks = max(it.n_tile0, it.n_tile1);
+  return it;
+}
+
 // 10 warps: three share a scheduler on two of the four sub-partitions (16,384 registers
 // each), which caps a thread at 168 registers; the softmax threads keep a 128-key score row
 // in registers within that.
+//
+// Persistent: one CTA per SM takes items from a global counter until they run out. The TMA
+// warp takes the next item as soon as it has issued the current one's loads and publishes it
+// through a small shared-memory queue; so the next item's Q and first K/V blocks load while
+// the current item's last blocks and its epilogue run, and its first products start as soon
+// as the tensor core is free.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -84,6 +125,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   using Cfg = AttnCfg<D>;
   constexpr int R = Cfg::kRing;
   constexpr int kDChunks = D / 64;
+  constexpr int kSched = 4;
   constexpr uint32_t kFmt = BF16 ? 1 : 0;
   constexpr uint32_t kIdescQK = make_idesc(1, kFmt, kFmt, 0, 0, 128, 128);
   constexpr uint32_t kIdescPV = make_idesc(1, kFmt, kFmt, 0, 1, 128, D);
@@ -94,39 +136,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sRing = sQ + Cfg::kQBytes;                   // [R][D/64 chunks][128 rows][128 B]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + R * Cfg::kTileBytes);
   uint64_t* q_full = bars;
-  uint64_t* ring_full = bars + 1;          // [R]
+  uint64_t* q_empty = q_full + 1;          // the item's last QK read Q
+  uint64_t* ring_full = q_empty + 1;       // [R]
   uint64_t* ring_empty = ring_full + R;    // [R]
   uint64_t* s_full = ring_empty + R;       // [2] QK_t done (and every MMA before it)
   uint64_t* p_full = s_full + 2;           // [2] softmax_t wrote P_t (128 arrivals)
   uint64_t* pv_done = p_full + 2;          // [2] PV_t done
-  uint64_t* drain = pv_done + 2;
+  uint64_t* sched_full = pv_done + 2;      // [kSched] item index published
+  uint64_t* sched_empty = sched_full + kSched;   // [kSched] read by the MMA warp and 8 softmax warps
+  uint64_t* drain = sched_empty + kSched;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* sched_item = reinterpret_cast<volatile int*>(tmem_slot + 2);   // [kSched]
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
 
-  const int pair = p.num_pairs - 1 - (int)blockIdx.x;   // heaviest causal pair first
-  const int bh = blockIdx.y;
-  const int b = bh / p.Hq;
-  const int h = bh - b * p.Hq;
-  const int hk = h / p.group;
-  const int q0 = pair * 256;
-  const int off = p.Skv - p.Sq;  // query q sees keys <= q + off
-  const int kv_blocks = (p.Skv + 127) / 128;
-  // Key blocks per query tile: under the causal mask tile 0 stops one block earlier than
-  // tile 1 whenever its last row's keys end before tile 1's; n_blocks = max over the tiles.
-  int n_tile0 = kv_blocks, n_tile1 = kv_blocks;
-  if (p.causal) {
-    const int last0 = min(q0 + 127, p.Sq - 1) + off;
-    const int last1 = min(q0 + 255, p.Sq - 1) + off;
-    n_tile0 = last0 < 0 ? 0 : min(kv_blocks, last0 / 128 + 1);
-    n_tile1 = last1 < 0 ? 0 : min(kv_blocks, last1 / 128 + 1);
-  }
-  const int n_blocks = max(n_tile0, n_tile1);
-
   if (threadIdx.x == 0) {
     bar_init(q_full, 1);
+    bar_init(q_empty, 1);
     for (int s = 0; s < R; ++s) {
       bar_init(&ring_full[s], 1);
       bar_init(&ring_empty[s], 1);
@@ -135,6 +163,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bar_init(&s_full[t], 1);
       bar_init(&p_full[t], 128);
       bar_init(&pv_done[t], 1);
+    }
+    for (int s = 0; s < kSched; ++s) {
+      bar_init(&sched_full[s], 1);
+      bar_init(&sched_empty[s], 9);
     }
     bar_init(drain, 1);
     *abort_flag = 0;
@@ -151,86 +183,129 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const WaitGuard g{p.status, abort_flag, p.timeout_ns};
 
   if (warp == 8) {
-    if (lane == 0 && n_blocks > 0) {
-      // ---------------- TMA producer: Q, then K_0, V_0, K_1, V_1, ... ----------------
+    if (lane == 0) {
+      // ---------------- scheduler + TMA producer ----------------
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      bar_arrive_expect_tx(q_full, Cfg::kQBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int c = 0; c < kDChunks; ++c)
-          tma_load_4d(sQ + t * Cfg::kTileBytes + c * kChunk, &tmQ, c * 64, q0 + 128 * t, h, b,
-                      q_full);
-      const int items = 2 * n_blocks;
-      int issued = 0;
-      for (int i = 0; i < items; ++i) {
-        const int slot = i % R;
-        const uint32_t par = (uint32_t)((i / R) & 1);
-        if (!wait_bar(&ring_empty[slot], par ^ 1, g, 11, i)) break;
-        bar_arrive_expect_tx(&ring_full[slot], Cfg::kTileBytes);
-        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
-        for (int c = 0; c < kDChunks; ++c)
-          tma_load_4d(sRing + slot * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128, hk,
-                      b, &ring_full[slot]);
-        issued = i + 1;
+      int rn = 0;      // ring items issued
+      int qi = 0;      // Q tiles issued
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k % kSched;
+        if (!wait_bar(&sched_empty[slot], (uint32_t)((k / kSched) & 1) ^ 1, g, 10, k)) {
+          ok = false;
+          break;
+        }
+        const int item = atomicAdd(p.work_counter, 1);
+        sched_item[slot] = item;
+        bar_arrive(&sched_full[slot]);            // release: the index is visible to waiters
+        if (item >= p.total_items) break;         // the end marker is published too
+        const AttnItem it = attn_item(item, p);
+        if (it.n_blocks == 0) continue;
+        // Q of this item once the previous item's last QK has read the old one.
+        if (!wait_bar(q_empty, (uint32_t)(qi & 1) ^ 1, g, 11, item)) { ok = false; break; }
+        bar_arrive_expect_tx(q_full, Cfg::kQBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int c = 0; c < kDChunks; ++c)
+            tma_load_4d(sQ + t * Cfg::kTileBytes + c * kChunk, &tmQ, c * 64, it.q0 + 128 * t,
+                        it.h, it.b, q_full);
+        ++qi;
+        for (int i = 0; i < 2 * it.n_blocks; ++i, ++rn) {
+          const int s = rn % R;
+          if (!wait_bar(&ring_empty[s], (uint32_t)((rn / R) & 1) ^ 1, g, 12, rn)) {
+            ok = false;
+            break;
+          }
+          bar_arrive_expect_tx(&ring_full[s], Cfg::kTileBytes);
+          const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+          for (int c = 0; c < kDChunks; ++c)
+            tma_load_4d(sRing + s * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128,
+                        it.hk, it.b, &ring_full[s]);
+        }
       }
-      if (*abort_flag) {
-        drain_wait_a(q_full, 0, p.timeout_ns);
-        for (int i = max(0, issued - R); i < issued; ++i)
+      if (!ok) {
+        // Let every copy this thread started land before the CTA's shared memory goes away.
+        if (qi > 0) drain_wait_a(q_full, (uint32_t)((qi - 1) & 1), p.timeout_ns);
+        for (int i = max(0, rn - R); i < rn; ++i)
           drain_wait_a(&ring_full[i % R], (uint32_t)((i / R) & 1), p.timeout_ns);
       }
     }
   } else if (warp == 9) {
-    if (n_blocks > 0) {
-      // ---------------- MMA issuer: the whole warp waits, one elected lane issues --------
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t r_base = smem_u32(sRing);
-      auto issue_qk = [&](int t, int slot) {
+    // ---------------- MMA issuer: the whole warp waits, one elected lane issues --------
+    const uint32_t q_base = smem_u32(sQ);
+    const uint32_t r_base = smem_u32(sRing);
+    auto issue_qk = [&](int t, int slot) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t o = (kk >> 2) * kChunk + (kk & 3) * 32;
-          const uint64_t ad = sdesc_sw128(q_base + t * Cfg::kTileBytes + o, 16, 1024);
-          const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + o, 16, 1024);
-          if (elect_one()) mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int t, int slot, bool acc) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA: P columns 8kk..8kk+7
-          // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64 dims
-          // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
-          const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
-                                          kChunk, 1024);
-          if (elect_one())
-            mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
-                       (acc || kk > 0) ? 1u : 0u);
-        }
-      };
-      auto n_tile = [&](int t) { return t ? n_tile1 : n_tile0; };
-      bool ok = wait_bar_warp(q_full, 0, g, 12, 0) && wait_bar_warp(&ring_full[0], 0, g, 13, 0);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t) {
-          if (n_tile(t) == 0) continue;
-          issue_qk(t, 0);
-          if (elect_one()) mma_commit(&s_full[t]);
-        }
-        if (elect_one()) mma_commit(&ring_empty[0]);  // K_0 (item 0)
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t o = (kk >> 2) * kChunk + (kk & 3) * 32;
+        const uint64_t ad = sdesc_sw128(q_base + t * Cfg::kTileBytes + o, 16, 1024);
+        const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + o, 16, 1024);
+        if (elect_one()) mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
       }
-      for (int j = 0; j < n_blocks && ok; ++j) {
-        const int iv = 2 * j + 1;             // V_j
-        const int ik = 2 * j + 2;             // K_{j+1}
-        const bool next = j + 1 < n_blocks;
-        if (!wait_bar_warp(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) break;
+    };
+    auto issue_pv = [&](int t, int slot, bool acc) {
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA: P columns 8kk..8kk+7
+        // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64 dims
+        // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
+        const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
+                                        kChunk, 1024);
+        if (elect_one())
+          mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
+                     (acc || kk > 0) ? 1u : 0u);
+      }
+    };
+    int rc = 0;               // ring items consumed before the current item
+    int qi = 0;               // items with work before the current one
+    int gt[2] = {0, 0};       // blocks of each tile before the current item
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int sslot = k % kSched;
+      if (!wait_bar_warp(&sched_full[sslot], (uint32_t)((k / kSched) & 1), g, 19, k)) break;
+      const int item = sched_item[sslot];
+      __syncwarp();
+      if (elect_one()) bar_arrive(&sched_empty[sslot]);
+      if (item >= p.total_items) break;
+      const AttnItem it = attn_item(item, p);
+      if (it.n_blocks == 0) continue;
+      const int nt[2] = {it.n_tile0, it.n_tile1};
+      const int nb = it.n_blocks;
+      if (!wait_bar_warp(q_full, (uint32_t)(qi & 1), g, 12, item) ||
+          !wait_bar_warp(&ring_full[rc % R], (uint32_t)((rc / R) & 1), g, 13, item)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int t = 0; t < 2; ++t) {
+        if (nt[t] == 0) continue;
+        issue_qk(t, rc % R);
+        if (elect_one()) mma_commit(&s_full[t]);
+      }
+      if (elect_one()) {
+        if (nb == 1) mma_commit(q_empty);         // the item's last QK has been issued
+        mma_commit(&ring_empty[rc % R]);          // K_0
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        const int iv = rc + 2 * j + 1;            // V_j
+        const int ik = rc + 2 * j + 2;            // K_{j+1}
+        const bool next = j + 1 < nb;
+        if (!wait_bar_warp(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) {
+          ok = false;
+          break;
+        }
         bool k_ready = false;
         for (int t = 0; t < 2 && ok; ++t) {
-          if (j < n_tile(t)) {
-            if (!wait_bar_warp(&p_full[t], (uint32_t)(j & 1), g, 15, j)) { ok = false; break; }
+          if (j < nt[t]) {
+            if (!wait_bar_warp(&p_full[t], (uint32_t)((gt[t] + j) & 1), g, 15, j)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
             issue_pv(t, iv % R, j > 0);
             if (elect_one()) mma_commit(&pv_done[t]);
           }
-          if (j + 1 < n_tile(t)) {
+          if (j + 1 < nt[t]) {
             if (!k_ready) {
               if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
                 ok = false;
@@ -243,136 +318,159 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         if (!ok) break;
-        if (elect_one()) mma_commit(&ring_empty[iv % R]);           // V_j done (both tiles)
+        if (elect_one()) {
+          if (j == nb - 2) mma_commit(q_empty);   // the item's last QK has been issued
+          mma_commit(&ring_empty[iv % R]);        // V_j done (both tiles)
+        }
         if (next) {
           if (!k_ready) {  // no tile used K_{j+1}: still consume it in order
-            if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) break;
+            if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
+              ok = false;
+              break;
+            }
           }
-          if (elect_one()) mma_commit(&ring_empty[ik % R]);         // K_{j+1} done
+          if (elect_one()) mma_commit(&ring_empty[ik % R]);   // K_{j+1} done
         }
       }
-      if (elect_one()) mma_commit(drain);
-      drain_wait_a(drain, 0, p.timeout_ns);
+      rc += 2 * nb;
+      gt[0] += nt[0];
+      gt[1] += nt[1];
+      ++qi;
     }
+    if (elect_one()) mma_commit(drain);
+    drain_wait_a(drain, 0, p.timeout_ns);
   } else {
     // ---------------- softmax, one warpgroup per query tile ----------------
     const int t = warp >> 2;
     const int wl = warp & 3;
     const int r = wl * 32 + lane;               // row within the tile = TMEM lane
-    const int q = q0 + 128 * t + r;             // query index
     const uint32_t lane_off = (uint32_t)(wl * 32) << 16;
     const uint32_t tS = tmem + lane_off + 128 * t;        // S_t, then P_t in its first 64 cols
     const uint32_t tO = tmem + lane_off + 256 + 128 * t;
     const float NEG_INF = -INFINITY;
-    float m_ref = NEG_INF;   // running max (log2 domain, scale folded in)
-    float l = 0.f;           // running sum of p relative to m_ref
+    const int off = p.Skv - p.Sq;
+    int gt = 0;               // blocks of this tile before the current item
     bool ok = true;
-    const int tile_first_row = q0 + 128 * t;
-    const int nt = t ? n_tile1 : n_tile0;   // key blocks this tile takes part in
+    for (int k = 0; ok; ++k) {
+      const int sslot = k % kSched;
+      if (!wait_bar(&sched_full[sslot], (uint32_t)((k / kSched) & 1), g, 20, k)) break;
+      const int item = sched_item[sslot];
+      __syncwarp();
+      if (lane == 0) bar_arrive(&sched_empty[sslot]);
+      if (item >= p.total_items) break;
+      const AttnItem it = attn_item(item, p);
+      const int b = it.b, h = it.h;
+      const int q = it.q0 + 128 * t + r;          // query index
+      float m_ref = NEG_INF;   // running max (log2 domain, scale folded in)
+      float l = 0.f;           // running sum of p relative to m_ref
+      const int tile_first_row = it.q0 + 128 * t;
+      const int nt = it.n_blocks == 0 ? 0 : (t ? it.n_tile1 : it.n_tile0);
 
-    for (int j = 0; j < nt; ++j) {
-      // S_t(j) ready; PV_t(j-1) (so O_t, and the P_t columns) is complete too.
-      if (!wait_bar(&s_full[t], (uint32_t)(j & 1), g, 21, j)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t s[128];
-      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
-      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
-      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
-      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
-      tmem_wait_ld();
+      for (int j = 0; j < nt; ++j) {
+        // S_t(j) ready; PV_t(j-1) (so O_t, and the P_t columns) is complete too.
+        if (!wait_bar(&s_full[t], (uint32_t)((gt + j) & 1), g, 21, j)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t s[128];
+        tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
+        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
+        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
+        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
+        tmem_wait_ld();
 
-      const int kbase = j * 128;
-      const bool need_mask =
-          (kbase + 127 >= p.Skv) || (p.causal && kbase + 127 > tile_first_row + off);
-      const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
-      auto mask = [&]() {
-        if (need_mask) {
+        const int kbase = j * 128;
+        const bool need_mask =
+            (kbase + 127 >= p.Skv) || (p.causal && kbase + 127 > tile_first_row + off);
+        const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
+        auto mask = [&]() {
+          if (need_mask) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
-        }
-      };
-      const float sl = p.scale_log2;
-      // p = 2^(s·scale·log2e - m) for the row, packed pairwise in place over s[0..63];
-      // returns the row sum (4 independent chains).
-      auto exps = [&](float m_use) {
-        float sump[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c = 0; c < 128; ++c)
+              if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
+          }
+        };
+        const float sl = p.scale_log2;
+        // p = 2^(s·scale·log2e - m) for the row, packed pairwise in place over s[0..63];
+        // returns the row sum (4 independent chains).
+        auto exps = [&](float m_use) {
+          float sump[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
-          sump[c & 3] += p0 + p1;
-          s[c] = pack2<BF16>(p0, p1);
-        }
-        return (sump[0] + sump[1]) + (sump[2] + sump[3]);
-      };
-      mask();
+          for (int c = 0; c < 64; ++c) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
+            sump[c & 3] += p0 + p1;
+            s[c] = pack2<BF16>(p0, p1);
+          }
+          return (sump[0] + sump[1]) + (sump[2] + sump[3]);
+        };
+        mask();
 
-      // Lazy rescaling needs the block's row max only when it exceeds the running max by
-      // more than 2^8. So from the second block on, exponentiate against the running max
-      // first: a row sum <= 256 proves every p <= 2^8 and the block is done. Otherwise
-      // (or on the first block, or for a row with no key yet) the warp reloads S from TMEM,
-      // takes the true max and recomputes; a row that passed the first test recomputes the
-      // same values.
-      float alpha = 1.f;
-      bool resc = false;
-      float sum = 0.f;
-      bool done = false;
-      if (j > 0) {
-        sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
-        done = (m_ref != NEG_INF) && (sum <= 256.f);
-      }
-      if (!__all_sync(0xffffffffu, done)) {
+        // Lazy rescaling needs the block's row max only when it exceeds the running max by
+        // more than 2^8. So from the second block on, exponentiate against the running max
+        // first: a row sum <= 256 proves every p <= 2^8 and the block is done. Otherwise
+        // (or on the first block, or for a row with no key yet) the warp reloads S from
+        // TMEM, takes the true max and recomputes; a row that passed the first test
+        // recomputes the same values.
+        float alpha = 1.f;
+        bool resc = false;
+        float sum = 0.f;
+        bool done = false;
         if (j > 0) {
-          tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
-          tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
-          tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
-          tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
-          tmem_wait_ld();
-          mask();
+          sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
+          done = (m_ref != NEG_INF) && (sum <= 256.f);
         }
-        // Row max as 4 independent chains (one chain would serialise 128 dependent maxes).
-        float mxp[4];
+        if (!__all_sync(0xffffffffu, done)) {
+          if (j > 0) {
+            tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
+            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
+            tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
+            tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
+            tmem_wait_ld();
+            mask();
+          }
+          // Row max as 4 independent chains (one chain would serialise 128 dependent maxes).
+          float mxp[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
+          for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
 #pragma unroll
-        for (int c = 4; c < 128; c += 4)
+          for (int c = 4; c < 128; c += 4)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
-        const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-        const float m_new = mx * sl;
-        if (j == 0) {
-          m_ref = m_new;
-        } else if (m_new > m_ref + 8.f) {
-          alpha = fast_exp2(m_ref - m_new);
-          m_ref = m_new;
-          resc = true;
+            for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
+          const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+          const float m_new = mx * sl;
+          if (j == 0) {
+            m_ref = m_new;
+          } else if (m_new > m_ref + 8.f) {
+            alpha = fast_exp2(m_ref - m_new);
+            m_ref = m_new;
+            resc = true;
+          }
+          sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
         }
-        sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
-      }
-      // P_t (64 packed columns) over the first half of S_t: the MMA's A operand.
-      tmem_st32(tS + 0, &s[0]);
-      tmem_st32(tS + 32, &s[32]);
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {
+        // P_t (64 packed columns) over the first half of S_t: the MMA's A operand.
+        tmem_st32(tS + 0, &s[0]);
+        tmem_st32(tS + 32, &s[32]);
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t o[16];
-          tmem_ld16(tO + 16 * c, o);
-          tmem_wait_ld();
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t o[16];
+            tmem_ld16(tO + 16 * c, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st16(tO + 16 * c, o);
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st16(tO + 16 * c, o);
+          }
         }
+        tmem_wait_st();
+        l = l * alpha + sum;
+        tc_fence_before();
+        bar_arrive(&p_full[t]);
       }
-      tmem_wait_st();
-      l = l * alpha + sum;
-      tc_fence_before();
-      bar_arrive(&p_full[t]);
-    }
+      if (!ok) break;
 
-    // ---------------- epilogue: O / l -> global, lse ----------------
-    if (ok && nt > 0) ok = wait_bar(&pv_done[t], (uint32_t)((nt - 1) & 1), g, 23, 0);
-    if (ok) {
+      // ---------------- epilogue: O / l -> global, lse ----------------
+      // O_t is rewritten by the next item's first P·V only after this warpgroup has
+      // produced that item's first P, i.e. after these loads have completed.
+      if (nt > 0 && !wait_bar(&pv_done[t], (uint32_t)((gt + nt - 1) & 1), g, 23, 0)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = q < p.Sq;
@@ -399,11 +497,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
         }
       }
+      tc_fence_before();
       if (p.lse && row_ok) {
         const float mu = (m_ref == NEG_INF) ? 0.f : m_ref;
         const float v = l > 0.f ? (mu + __log2f(l)) * 0.69314718055994530942f : NEG_INF;
         p.lse[((long long)b * p.Hq + h) * p.Sq + q] = v;
       }
+      gt += nt;
     }
   }
 
@@ -450,13 +550,12 @@ void packed_or(const int64_t* s, int64_t H, int64_t S, int64_t D, long long out[
 
 template <int D, bool BF16>
 int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                const AttnParams& p, cudaStream_t stream) {
+                const AttnParams& p, int ctas, cudaStream_t stream) {
   auto kern = attn_fwd_kernel<D, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        AttnCfg<D>::kSmem);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "cudaFuncSetAttribute");
-  dim3 grid(p.num_pairs, p.B * p.Hq);
-  kern<<<grid, kAttnThreads, AttnCfg<D>::kSmem, stream>>>(tq, tk, tv, p);
+  kern<<<ctas, kAttnThreads, AttnCfg<D>::kSmem, stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "kernel launch");
   return LVB_OK;
@@ -522,14 +621,32 @@ int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void
   p.lse = lse;
   p.status = dev->status;
   p.timeout_ns = wait_timeout_ns();
-  if (p.num_pairs > 2147483647 || B * Hq > 65535)
-    return fail(LVB_ERR_UNSUPPORTED, op, "batch*heads above 65535", "split the batch");
+  const long long items = (long long)p.num_pairs * B * Hq;
+  if (items > 2147483647LL - 4096)
+    return fail(LVB_ERR_UNSUPPORTED, op, "more than 2^31 query-tile pairs", "split the batch");
+  p.total_items = (int)items;
+  const int ctas = (int)std::min<long long>(items, std::max(1, dev->sm_count));
+  // The item counter: zeroed on the stream before the launch, freed after it.
+  void* ws = nullptr;
+  cudaError_t e = workspace_alloc(dev, &ws, 16, stream);
+  if (e != cudaSuccess) return fail_cuda(e, op, "work counter allocation");
+  p.work_counter = reinterpret_cast<int*>(ws);
+  e = cudaMemsetAsync(ws, 0, 16, stream);
+  int st = e == cudaSuccess ? LVB_OK : fail_cuda(e, op, "work counter reset");
   const bool bf16 = d->dtype == LVB_BF16;
-  if (D == 128) return bf16 ? launch_attn<128, true>(tq, tk, tv, p, stream)
-                            : launch_attn<128, false>(tq, tk, tv, p, stream);
-  if (D == 64) return bf16 ? launch_attn<64, true>(tq, tk, tv, p, stream)
-                           : launch_attn<64, false>(tq, tk, tv, p, stream);
-  return fail(LVB_ERR_UNSUPPORTED, op, "head_dim must be 64 or 128");
+  if (st == LVB_OK) {
+    if (D == 128)
+      st = bf16 ? launch_attn<128, true>(tq, tk, tv, p, ctas, stream)
+                : launch_attn<128, false>(tq, tk, tv, p, ctas, stream);
+    else if (D == 64)
+      st = bf16 ? launch_attn<64, true>(tq, tk, tv, p, ctas, stream)
+                : launch_attn<64, false>(tq, tk, tv, p, ctas, stream);
+    else
+      st = fail(LVB_ERR_UNSUPPORTED, op, "head_dim must be 64 or 128");
+  }
+  e = cudaFreeAsync(ws, stream);
+  if (st == LVB_OK && e != cudaSuccess) return fail_cuda(e, op, "work counter free");
+  return st;
 }
 
 }  // namespace lvb
