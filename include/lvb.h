@@ -249,8 +249,8 @@ typedef enum lvb_attn_kernel {
   LVB_ATTN_FLASH = 0,   /* persistent CTAs, two 128-row query tiles per work item, keys
                            streamed in 128-key blocks */
   LVB_ATTN_DECODE = 1,  /* few query rows per KV head (group·seq_q <= 32, head_dim 128): the
-                           KV cache streamed once, split over the keys; the CTA that finishes
-                           a (batch, KV head)'s last split merges them */
+                           KV cache streamed once, split over the keys, the splits merged
+                           by a second kernel */
   LVB_ATTN_EMPTY = 2    /* seq_kv == 0: O = 0, lse = -inf */
 } lvb_attn_kernel;
 

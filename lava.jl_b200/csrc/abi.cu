@@ -625,7 +625,7 @@ int lvb_attention_plan_for(const lvb_attn_desc* d, int32_t sm_count, lvb_attn_pl
     out->kernel = LVB_ATTN_DECODE;
     out->splits = ns;
     out->ctas = ctas;
-    out->launches = 1;   // the last split of each (batch, KV head) merges in the same kernel
+    out->launches = ns > 1 ? 2 : 1;   // + the merge of the splits
     return LVB_OK;
   }
   out->kernel = LVB_ATTN_FLASH;

@@ -9,9 +9,8 @@
 //   Sᵀ (128 keys × NR rows) = K_j (128 × D) · Qᵀ,   Oᵀ (D × NR) += V_jᵀ · P_jᵀ
 // with NR = 16 or 32 ≥ group·seq_q (the rows of one KV head's query heads and positions).
 //   * work item = (batch, KV head, key range); a key range of a long cache is split so that
-//     every SM streams; each split writes its partial (O, max, sum) and the CTA that finishes
-//     the last split of a (batch, KV head) merges them (flash-decoding, no second launch); a
-//     single split writes O directly;
+//     every SM streams; partial (O, max, sum) of the splits are merged by a second kernel
+//     (flash-decoding); a single split writes O directly;
 //   * persistent CTAs, 192 threads: warps 0-3 softmax and epilogue (thread = key of the block
 //     for Sᵀ, = head-dim element for Oᵀ), warp 4 TMA (Q of the item, then K_j, V_j through a
 //     6-slot ring, running ahead across items), warp 5 MMA (QK_j into one of two Sᵀ
@@ -46,7 +45,6 @@ struct DecParams {
   float* lse;
   float* part;              // [items][NR][D] unnormalised O (nsplit > 1)
   float* part_ml;           // [items][NR][2] (max in log2 units, sum)
-  int* done;                // [B·Hkv] splits finished (zero at launch)
   DevStatus* status;
   unsigned long long timeout_ns;
 };
@@ -97,35 +95,6 @@ __device__ __forceinline__ void item_coords(int item, const DecParams& p, int& b
   kb1 = min(nkb, kb0 + p.bps);
 }
 
-// Merge the splits of one (batch, KV head) for row r, head-dim element t:
-// O = Σ 2^(m_s - m) O_s / Σ 2^(m_s - m) l_s with m = max m_s, in split order (the same bits
-// whichever CTA merges). The partials come from other SMs: read through L2.
-template <int NR, bool BF16>
-__device__ __forceinline__ void merge_splits(const DecParams& p, int bh, int r, int t) {
-  const int b = bh / p.Hkv, hk = bh - b * p.Hkv;
-  const long long item0 = (long long)bh * p.nsplit;
-  float m = -INFINITY;
-  for (int s = 0; s < p.nsplit; ++s) m = fmaxf(m, __ldcg(&p.part_ml[((item0 + s) * NR + r) * 2]));
-  float num = 0.f, den = 0.f;
-  if (m != -INFINITY) {
-    for (int s = 0; s < p.nsplit; ++s) {
-      const float ms = __ldcg(&p.part_ml[((item0 + s) * NR + r) * 2]);
-      if (ms == -INFINITY) continue;
-      const float w = fast_exp2(ms - m);
-      num += w * __ldcg(&p.part[((item0 + s) * NR + r) * kDecD + t]);
-      den += w * __ldcg(&p.part_ml[((item0 + s) * NR + r) * 2 + 1]);
-    }
-  }
-  const int hq = hk * p.group + r / p.Sq;
-  const int sq = r % p.Sq;
-  uint16_t* dst = reinterpret_cast<uint16_t*>(p.O) + (long long)b * p.o_sb +
-                  (long long)hq * p.o_sh + (long long)sq * p.o_ss;
-  dst[t] = to_bits16<BF16>(den > 0.f ? num / den : 0.f);
-  if (p.lse && t == 0)
-    p.lse[((long long)b * p.Hq + hq) * p.Sq + sq] =
-        den > 0.f ? (m + __log2f(den)) * 0.69314718055994530942f : -INFINITY;
-}
-
 template <int NR, bool BF16>
 __global__ void __launch_bounds__(kDecThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -156,7 +125,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   uint64_t* drain = o_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -442,20 +410,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           }
         }
       }
-      if (p.nsplit > 1) {
-        const int bh = item / p.nsplit;
-        // The last split of a (batch, KV head) to finish merges all of them: every thread
-        // makes its partial writes visible, then one thread counts this split in.
-        __threadfence();
-        named_barrier_sync(1, 128);
-        if (t == 0) *last_flag = atomicAdd(&p.done[bh], 1) == p.nsplit - 1 ? 1 : 0;
-        named_barrier_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          for (int r = 0; r < p.nrows; ++r) merge_splits<NR, BF16>(p, bh, r, t);
-        }
-      }
-      // The sums' slots (and the flag) are rewritten by the next item only after barrier 1.
+      // The sums' slots are rewritten by the next item's first block only after barrier 1.
       named_barrier_sync(1, 128);
     }
     (void)ok;
@@ -469,6 +424,36 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   }
 }
 
+// Merge the splits of one (batch, KV head): O = Σ 2^(m_s - m) O_s / Σ 2^(m_s - m) l_s.
+template <int NR, bool BF16>
+__global__ void attn_decode_combine_kernel(const DecParams p) {
+  const int bh = blockIdx.x;           // batch·Hkv + KV head
+  const int r = blockIdx.y;            // row within the group
+  const int t = threadIdx.x;           // head-dim element
+  const int b = bh / p.Hkv, hk = bh - b * p.Hkv;
+  const long long item0 = (long long)bh * p.nsplit;
+  float m = -INFINITY;
+  for (int s = 0; s < p.nsplit; ++s) m = fmaxf(m, p.part_ml[((item0 + s) * NR + r) * 2]);
+  float num = 0.f, den = 0.f;
+  if (m != -INFINITY) {
+    for (int s = 0; s < p.nsplit; ++s) {
+      const float ms = p.part_ml[((item0 + s) * NR + r) * 2];
+      if (ms == -INFINITY) continue;
+      const float w = fast_exp2(ms - m);
+      num += w * p.part[((item0 + s) * NR + r) * kDecD + t];
+      den += w * p.part_ml[((item0 + s) * NR + r) * 2 + 1];
+    }
+  }
+  const int hq = hk * p.group + r / p.Sq;
+  const int sq = r % p.Sq;
+  uint16_t* dst = reinterpret_cast<uint16_t*>(p.O) + (long long)b * p.o_sb +
+                  (long long)hq * p.o_sh + (long long)sq * p.o_ss;
+  dst[t] = to_bits16<BF16>(den > 0.f ? num / den : 0.f);
+  if (p.lse && t == 0)
+    p.lse[((long long)b * p.Hq + hq) * p.Sq + sq] =
+        den > 0.f ? (m + __log2f(den)) * 0.69314718055994530942f : -INFINITY;
+}
+
 template <int NR, bool BF16>
 int launch_decode(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                   const DecParams& p, int ctas, cudaStream_t stream) {
@@ -479,6 +464,12 @@ int launch_decode(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMa
   kern<<<ctas, kDecThreads, DecCfg<NR>::kSmem, stream>>>(tq, tk, tv, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "decode launch");
+  if (p.nsplit > 1) {
+    dim3 grid(p.B * p.Hkv, p.nrows);
+    attn_decode_combine_kernel<NR, BF16><<<grid, kDecD, 0, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "decode combine launch");
+  }
   return LVB_OK;
 }
 
@@ -565,18 +556,11 @@ int attn_decode_launch(const lvb_attn_desc* d, const long long qs[3], const long
   const int NR = nrows <= 16 ? 16 : 32;
   void* ws = nullptr;
   if (p.nsplit > 1) {
-    const size_t part_bytes = (size_t)p.items * NR * (kDecD + 2) * sizeof(float);
-    const size_t done_bytes = (size_t)p.B * p.Hkv * sizeof(int);
-    cudaError_t e = workspace_alloc(dev, &ws, part_bytes + done_bytes, stream);
+    const size_t bytes = (size_t)p.items * NR * (kDecD + 2) * sizeof(float);
+    cudaError_t e = workspace_alloc(dev, &ws, bytes, stream);
     if (e != cudaSuccess) return fail_cuda(e, op, "decode workspace allocation");
     p.part = reinterpret_cast<float*>(ws);
     p.part_ml = p.part + (size_t)p.items * NR * kDecD;
-    p.done = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + part_bytes);
-    e = cudaMemsetAsync(p.done, 0, done_bytes, stream);
-    if (e != cudaSuccess) {
-      cudaFreeAsync(ws, stream);
-      return fail_cuda(e, op, "decode split counters reset");
-    }
   }
   const bool bf16 = d->dtype == LVB_BF16;
   int st;

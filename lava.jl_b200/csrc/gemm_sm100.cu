@@ -1041,6 +1041,17 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
+  if (d->K > 0 && gemv_applies(d)) {
+    // A matrix-vector product: the streaming kernel reads any alignment and layout in place
+    // and runs without its k split (whose partial sums would need a workspace), so nothing
+    // is copied or allocated. It has no waits, so no status word to clear.
+    DeviceState local;
+    local.device = device;
+    local.sm_count = sms;
+    local.status = reinterpret_cast<DevStatus*>(scratch);
+    return gemv_launch(d, nullptr, A, B, C, s, &local, /*allow_workspace=*/false);
+  }
+
   lvb_gemm_plan plan;
   st = gemm_plan_c(d, sms,
                    (uintptr_t)C % 16 == 0 && (d->ldc * dtype_size(d->c_type)) % 16 == 0, &plan);
@@ -1066,14 +1077,6 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   if (d->K == 0) return gemm_zero_fill(d, C, s);
 
   DeviceState local;  // no allocation: the status word is the scratch head
-  if (gemv_applies(d)) {
-    // A matrix-vector product: the streaming kernel without its k split (whose partial sums
-    // would need a workspace), so nothing is allocated.
-    local.device = device;
-    local.sm_count = sms;
-    local.status = status;
-    return gemv_launch(d, nullptr, A, B, C, s, &local, /*allow_workspace=*/false);
-  }
   local.device = device;
   local.sm_count = sms;
   local.status = status;

@@ -274,7 +274,7 @@ def test_attention_plans(lvb):
     """Few query rows per KV head take the decoding kernel, split over a long cache; long
     query sequences the flash kernel; an empty key sequence the fill kernel."""
     p = lvb.attention_plan(8, 64, 8, 1, 16384)              # C5's cache, one new token
-    assert p.kernel == lvb.ATTN_DECODE and p.splits > 1 and p.launches == 1 and p.ctas == 148
+    assert p.kernel == lvb.ATTN_DECODE and p.splits > 1 and p.launches == 2 and p.ctas == 148
     p = lvb.attention_plan(64, 32, 32, 1, 2048)              # many heads: no split needed
     assert p.kernel == lvb.ATTN_DECODE and p.splits == 1 and p.launches == 1
     assert lvb.attention_plan(1, 32, 1, 1, 300).kernel == lvb.ATTN_DECODE   # 32 rows
