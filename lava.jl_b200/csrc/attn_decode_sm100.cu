@@ -418,32 +418,83 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // This CTA has stored all it will: the merge kernel may be scheduled (it still waits for
+  // the whole grid's results before reading them).
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == kDecMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
   }
 }
 
-// Merge the splits of one (batch, KV head): O = Σ 2^(m_s - m) O_s / Σ 2^(m_s - m) l_s.
+constexpr int kMaxSplits = 1024;
+
+// Merge the splits of one (batch, KV head) row: O = Σ 2^(m_s - m) O_s / Σ 2^(m_s - m) l_s,
+// m = max m_s. One CTA per (batch·KV head, row), thread = head-dim element: the splits'
+// (max, sum) pairs are read one per thread and reduced through shared memory, then every
+// thread streams its column of the partial outputs with independent loads. Launched as a
+// programmatic dependent of the decode kernel: it is scheduled while the decode kernel ends
+// and waits (griddepcontrol.wait) for its results before reading them.
 template <int NR, bool BF16>
-__global__ void attn_decode_combine_kernel(const DecParams p) {
+__global__ void __launch_bounds__(kDecD) attn_decode_combine_kernel(const DecParams p) {
+  __shared__ float w[kMaxSplits];
+  __shared__ float red[kDecD / 32];
+  __shared__ float bcast;
   const int bh = blockIdx.x;           // batch·Hkv + KV head
   const int r = blockIdx.y;            // row within the group
   const int t = threadIdx.x;           // head-dim element
+  const int lane = t & 31, wp = t >> 5;
   const int b = bh / p.Hkv, hk = bh - b * p.Hkv;
   const long long item0 = (long long)bh * p.nsplit;
-  float m = -INFINITY;
-  for (int s = 0; s < p.nsplit; ++s) m = fmaxf(m, p.part_ml[((item0 + s) * NR + r) * 2]);
-  float num = 0.f, den = 0.f;
-  if (m != -INFINITY) {
-    for (int s = 0; s < p.nsplit; ++s) {
-      const float ms = p.part_ml[((item0 + s) * NR + r) * 2];
-      if (ms == -INFINITY) continue;
-      const float w = fast_exp2(ms - m);
-      num += w * p.part[((item0 + s) * NR + r) * kDecD + t];
-      den += w * p.part_ml[((item0 + s) * NR + r) * 2 + 1];
-    }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the splits' maxima, one per thread (strided), reduced to m
+  float mloc = -INFINITY;
+  for (int s = t; s < p.nsplit; s += kDecD) {
+    const float ms = p.part_ml[((item0 + s) * NR + r) * 2];
+    w[s] = ms;
+    mloc = fmaxf(mloc, ms);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+  if (lane == 0) red[wp] = mloc;
+  __syncthreads();
+  if (t == 0) {
+    float m = red[0];
+    for (int i = 1; i < kDecD / 32; ++i) m = fmaxf(m, red[i]);
+    bcast = m;
+  }
+  __syncthreads();
+  const float m = bcast;
+  // weights 2^(m_s - m) in shared memory, and the weighted sum of the splits' row sums
+  float dloc = 0.f;
+  for (int s = t; s < p.nsplit; s += kDecD) {
+    const float ms = w[s];
+    const float ws = (m == -INFINITY || ms == -INFINITY) ? 0.f : fast_exp2(ms - m);
+    w[s] = ws;
+    dloc += ws * p.part_ml[((item0 + s) * NR + r) * 2 + 1];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dloc += __shfl_xor_sync(0xffffffffu, dloc, o);
+  __syncthreads();   // every w[s] written; red reused
+  if (lane == 0) red[wp] = dloc;
+  __syncthreads();
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < kDecD / 32; ++i) den += red[i];
+  // the weighted partial outputs, in split order
+  float num = 0.f;
+  const float* col = p.part + (item0 * NR + r) * kDecD + t;
+  const long long stride = (long long)NR * kDecD;
+  int s = 0;
+  for (; s + 4 <= p.nsplit; s += 4) {
+    const float v0 = col[(s + 0) * stride], v1 = col[(s + 1) * stride];
+    const float v2 = col[(s + 2) * stride], v3 = col[(s + 3) * stride];
+    num += w[s] * v0;
+    num += w[s + 1] * v1;
+    num += w[s + 2] * v2;
+    num += w[s + 3] * v3;
+  }
+  for (; s < p.nsplit; ++s) num += w[s] * col[s * stride];
   const int hq = hk * p.group + r / p.Sq;
   const int sq = r % p.Sq;
   uint16_t* dst = reinterpret_cast<uint16_t*>(p.O) + (long long)b * p.o_sb +
@@ -465,10 +516,17 @@ int launch_decode(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMa
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "decode launch");
   if (p.nsplit > 1) {
-    dim3 grid(p.B * p.Hkv, p.nrows);
-    attn_decode_combine_kernel<NR, BF16><<<grid, kDecD, 0, stream>>>(p);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "decode combine launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.B * p.Hkv, p.nrows);
+    cfg.blockDim = dim3(kDecD);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, attn_decode_combine_kernel<NR, BF16>, p);
+    if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "decode merge launch");
   }
   return LVB_OK;
 }
@@ -501,6 +559,7 @@ void attn_decode_plan(const lvb_attn_desc* d, int sm_count, int* nsplit, int* bp
     const double eff = (double)items / (double)(rounds * c);
     if (eff > best_eff + 1e-9) { best_eff = eff; best_ns = real_ns; }
   }
+  best_ns = std::min<long long>(best_ns, kMaxSplits);
   const int b = (int)((nkb + best_ns - 1) / best_ns);
   *nsplit = (int)((nkb + b - 1) / b);
   *bps = b;
