@@ -285,6 +285,40 @@ __device__ __forceinline__ void store_staged(const CUtensorMap* tmD, const uint3
   ++cnt;
 }
 
+// Staged store of a pair of chunks for 16-bit outputs: the warp's 32 (m) × 64 (n) sub-tile
+// is one 4 KB box {64 n, 32 m} of 128-byte rows (128B swizzle: 16-byte chunk j of row r at
+// j ^ (r & 7)), one fence and one TMA tensor store for two chunks. The first chunk fills the
+// left half of each row, the second the right half. Two 4 KB buffers per warp.
+template <int OUT>
+__device__ __forceinline__ void stage_half16(const uint32_t (&r)[32], uint32_t sbase,
+                                             uint32_t cnt, int half) {
+  const uint32_t lane = lane_id();
+  const uint32_t buf = sbase + (cnt & 1) * kStoreBufBytes;
+  if (half == 0) {
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+  }
+  const uint32_t row = buf + lane * 128;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    st_shared_v4(row + (((4 * half + c) ^ (lane & 7)) << 4), pack_out2<OUT>(r[8 * c], r[8 * c + 1]),
+                 pack_out2<OUT>(r[8 * c + 2], r[8 * c + 3]),
+                 pack_out2<OUT>(r[8 * c + 4], r[8 * c + 5]),
+                 pack_out2<OUT>(r[8 * c + 6], r[8 * c + 7]));
+}
+
+__device__ __forceinline__ void commit_pair16(const CUtensorMap* tmD, uint32_t sbase,
+                                              uint32_t& cnt, int m0w, int n0) {
+  const uint32_t buf = sbase + (cnt & 1) * kStoreBufBytes;
+  fence_proxy_async_smem();  // this thread's writes -> visible to the TMA (async proxy)
+  __syncwarp();
+  if (lane_id() == 0) {
+    tma_store_2d(tmD, buf, n0, m0w);
+    bulk_commit_group();
+  }
+  ++cnt;
+}
+
 // Drains this warp's 32 TMEM lanes of one accumulator (NCH chunks of 32 columns): the
 // tcgen05.ld of chunk c+1 is in flight while chunk c goes through the epilogue and its
 // stores, so the TMEM round trip is hidden. `release` hands the accumulator back as soon as
@@ -295,15 +329,27 @@ __device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap
                                           float bias_m, uint32_t s_out, uint32_t& n_staged,
                                           Release release) {
   static_assert(NCH % 2 == 0, "chunks are drained in pairs");
+  constexpr bool k16 = OUT == OUT_F16 || OUT == OUT_BF16;
   const bool m_ok = m < p.M;
   uint32_t ra[32], rb[32];
   auto handle = [&](uint32_t (&r)[32], int c) {
     const int n0 = n_base + c * 32;
     if (p.epi) apply_epilogue<OUT>(p, r, m, n0, m_ok ? min(32, p.N - n0) : 0, bias_m);
-    if (p.stage_out && m0w + 32 <= p.M && n0 + 32 <= p.N)
-      store_staged<OUT>(tmD, r, s_out, n_staged, m0w, n0);
-    else if (m_ok)
-      store_direct<OUT>(p, r, m, n0);
+    if constexpr (k16) {
+      // 16-bit outputs go out as 32 x 64 boxes: chunk c (even) and c + 1 share one store
+      const int np = n_base + (c & ~1) * 32;
+      if (p.stage_out && m0w + 32 <= p.M && np + 64 <= p.N) {
+        stage_half16<OUT>(r, s_out, n_staged, c & 1);
+        if (c & 1) commit_pair16(tmD, s_out, n_staged, m0w, np);
+      } else if (m_ok) {
+        store_direct<OUT>(p, r, m, n0);
+      }
+    } else {
+      if (p.stage_out && m0w + 32 <= p.M && n0 + 32 <= p.N)
+        store_staged<OUT>(tmD, r, s_out, n_staged, m0w, n0);
+      else if (m_ok)
+        store_direct<OUT>(p, r, m, n0);
+    }
     __syncwarp();  // tcgen05.ld / wait are .sync.aligned: reconverge after the stores
   };
   tmem_ld32(t_row, ra);
@@ -1178,16 +1224,17 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
                             plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
   if (st) return st;
   // Kernel-space D is n-contiguous when the plan oriented the product that way (C can take
-  // TMA stores); its interior 32×32 boxes then go out through TMA tensor stores with the
-  // row swizzle the epilogue writes (64B for 16-bit, 128B for 32-bit elements).
+  // TMA stores); its interior boxes (32 m × 64 n of 16-bit or 32 m × 32 n of 32-bit
+  // elements: rows of 128 bytes) then go out through TMA tensor stores with the 128B row
+  // swizzle the epilogue writes.
   const int osize = dtype_size(d->c_type);
   const int d_nmajor = (plan.swap_ab != 0) != (d->c_rowmajor != 0);
   CUtensorMap td;
   std::memset(&td, 0, sizeof td);
   int stage_out = 0;
   if (d_nmajor) {
-    if (make_tmap_2d_sw(&td, C, osize, (uint64_t)kN, (uint64_t)kM, (uint64_t)d->ldc, 32, 32,
-                        osize == 2 ? 64 : 128, "lvb_gemm") == LVB_OK)
+    if (make_tmap_2d_sw(&td, C, osize, (uint64_t)kN, (uint64_t)kM, (uint64_t)d->ldc,
+                        osize == 2 ? 64 : 32, 32, 128, "lvb_gemm") == LVB_OK)
       stage_out = 1;
     else
       clear_error();   // direct stores in the same orientation: correct, slower
