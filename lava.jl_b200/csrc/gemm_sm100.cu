@@ -84,6 +84,22 @@ template <typename T>
 __device__ __forceinline__ void add_loaded32(const void* base, long long i0, long long stride,
                                              int nv, float (&out)[32]) {
   const T* x = reinterpret_cast<const T*>(base) + i0;
+  if (stride == 1 && nv == 32 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // A contiguous run (a bias slice, or a residual row when D is n-contiguous): 16-byte
+    // loads marked for streaming (evict-first), so the residual does not push the A and B
+    // panels the next tiles re-read out of L2.
+    constexpr int E = 16 / (int)sizeof(T);
+    uint4 w[32 / E];
+#pragma unroll
+    for (int i = 0; i < 32 / E; ++i) w[i] = __ldcs(reinterpret_cast<const uint4*>(x) + i);
+#pragma unroll
+    for (int i = 0; i < 32 / E; ++i) {
+      const T* e = reinterpret_cast<const T*>(&w[i]);
+#pragma unroll
+      for (int k = 0; k < E; ++k) out[i * E + k] += to_f32(e[k]);
+    }
+    return;
+  }
   T v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = j < nv ? x[j * stride] : T(0.f);
