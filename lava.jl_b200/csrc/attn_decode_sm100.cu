@@ -21,6 +21,7 @@
 //     product; Vᵀ is read MN-major straight from the V block.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 #include "lvb_internal.h"
 
@@ -54,7 +55,7 @@ struct DecCfg {
   static constexpr int kQBytes = 2 * NR * 128;        // two 64-dim chunks of NR rows
   static constexpr int kPBytes = 2 * NR * 128;        // two 64-key chunks of NR rows
   static constexpr int kTmemCols = NR == 16 ? 64 : 128;
-  static constexpr int kSmem = kDecRing * kDecBlockBytes + kQBytes + 2 * kPBytes + 2 * 4 * NR * 4 +
+  static constexpr int kSmem = kDecRing * kDecBlockBytes + 2 * kQBytes + 2 * kPBytes + 2 * 4 * NR * 4 +
                                512 + 1024;
 };
 
@@ -74,13 +75,15 @@ __device__ __forceinline__ void dec_drain(uint64_t* bar, uint32_t parity, uint64
 
 template <int NR>
 __device__ __forceinline__ void tmem_ld_nr(uint32_t taddr, uint32_t (&r)[NR]) {
-  if constexpr (NR == 16) tmem_ld16(taddr, r);
+  if constexpr (NR == 8) tmem_ld8(taddr, r);
+  else if constexpr (NR == 16) tmem_ld16(taddr, r);
   else tmem_ld32(taddr, r);
 }
 
 template <int NR>
 __device__ __forceinline__ void tmem_st_nr(uint32_t taddr, uint32_t (&r)[NR]) {
-  if constexpr (NR == 16) tmem_st16(taddr, r);
+  if constexpr (NR == 8) tmem_st8(taddr, r);
+  else if constexpr (NR == 16) tmem_st16(taddr, r);
   else tmem_st32(taddr, r);
 }
 
@@ -95,7 +98,10 @@ __device__ __forceinline__ void item_coords(int item, const DecParams& p, int& b
   kb1 = min(nkb, kb0 + p.bps);
 }
 
-template <int NR, bool BF16>
+// NR: the N of the products (16 or 32, the tensor core's minimum is 16 for 128 rows); RR <= NR:
+// the rows the softmax works on (8 when the group has at most 8 query rows: the other
+// columns of Sᵀ, Pᵀ and Oᵀ are computed but never read).
+template <int NR, int RR, bool BF16>
 __global__ void __launch_bounds__(kDecThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const DecParams p) {
@@ -108,15 +114,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* sRing = smem;                                  // [R][2 chunks][128 keys][128 B]
-  uint8_t* sQ = sRing + R * kDecBlockBytes;               // [2 chunks][NR rows][128 B]
-  uint8_t* sP = sQ + Cfg::kQBytes;                        // [2 bufs][2 chunks][NR rows][128 B]
+  uint8_t* sQ = sRing + R * kDecBlockBytes;               // [2 bufs][2 chunks][NR rows][128 B]
+  uint8_t* sP = sQ + 2 * Cfg::kQBytes;                    // [2 bufs][2 chunks][NR rows][128 B]
   float* sRed = reinterpret_cast<float*>(sP + 2 * Cfg::kPBytes);   // [2][4 warps][NR]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRed + 2 * 4 * NR);
   uint64_t* kv_full = bars;              // [R]
   uint64_t* kv_empty = kv_full + R;      // [R]
-  uint64_t* q_full = kv_empty + R;
-  uint64_t* q_empty = q_full + 1;
-  uint64_t* s_full = q_empty + 1;        // [2]
+  uint64_t* q_full = kv_empty + R;       // [2] Q buffers: item it uses buffer it & 1, so the
+  uint64_t* q_empty = q_full + 2;        // [2] next item's Q loads while this one runs
+  uint64_t* s_full = q_empty + 2;        // [2]
   uint64_t* s_empty = s_full + 2;        // [2] (128 arrivals)
   uint64_t* p_full = s_empty + 2;        // [2] (128 arrivals)
   uint64_t* p_empty = p_full + 2;        // [2] PV of that buffer done
@@ -134,8 +140,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       bar_init(&kv_full[s], 1);
       bar_init(&kv_empty[s], 1);
     }
-    bar_init(q_full, 1);
-    bar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      bar_init(&q_full[i], 1);
+      bar_init(&q_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       bar_init(&s_full[i], 1);
       bar_init(&s_empty[i], 128);
@@ -174,10 +182,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         int b, hk, kb0, kb1;
         item_coords(item, p, b, hk, kb0, kb1);
         // Q of the item once the previous item's last QK has read the old one.
-        if (!wait_bar(q_empty, (uint32_t)(it & 1) ^ 1, g, 51, item)) { ok = false; break; }
-        bar_arrive_expect_tx(q_full, 2 * p.nrows * 128);   // the box holds the real rows
+        const int qb = it & 1;
+        if (!wait_bar(&q_empty[qb], (uint32_t)((it >> 1) & 1) ^ 1, g, 51, item)) {
+          ok = false;
+          break;
+        }
+        bar_arrive_expect_tx(&q_full[qb], 2 * p.nrows * 128);   // the box holds the real rows
         for (int c = 0; c < 2; ++c)
-          tma_load_4d(sQ + c * NR * 128, &tmQ, c * 64, 0, hk * p.group, b, q_full);
+          tma_load_4d(sQ + qb * Cfg::kQBytes + c * NR * 128, &tmQ, c * 64, 0, hk * p.group, b,
+                      &q_full[qb]);
         ++q_loads;
         for (int kb = kb0; kb < kb1 && ok; ++kb) {
           for (int v = 0; v < 2; ++v, ++n) {
@@ -198,7 +211,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // Let the copies this thread started land before the CTA's shared memory goes away.
         for (int i = max(0, n - R); i < n; ++i)
           dec_drain(&kv_full[i % R], (uint32_t)((i / R) & 1), p.timeout_ns);
-        if (q_loads > 0) dec_drain(q_full, (uint32_t)((q_loads - 1) & 1), p.timeout_ns);
+        for (int i = max(0, q_loads - 2); i < q_loads; ++i)
+          dec_drain(&q_full[i & 1], (uint32_t)((i >> 1) & 1), p.timeout_ns);
       }
     }
   } else if (warp == kDecMmaWarp) {
@@ -217,7 +231,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       int b, hk, kb0, kb1;
       item_coords(item, p, b, hk, kb0, kb1);
       const int nb = kb1 - kb0;   // >= 1: the planner makes no empty split
-      if (!wait_bar_warp(q_full, (uint32_t)(it & 1), g, 53, item)) { ok = false; break; }
+      const int qb = it & 1;
+      if (!wait_bar_warp(&q_full[qb], (uint32_t)((it >> 1) & 1), g, 53, item)) { ok = false; break; }
       for (int j = 0; j <= nb && ok; ++j) {
         if (j < nb) {
           const int gj = gb + j;
@@ -230,13 +245,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t o = (kk >> 2) * kDecChunk + (kk & 3) * 32;
             const uint64_t ad = sdesc_sw128(r_base + sk * kDecBlockBytes + o, 16, 1024);
-            const uint64_t bd = sdesc_sw128(q_base + (kk >> 2) * NR * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(q_base + qb * Cfg::kQBytes + (kk >> 2) * NR * 128 +
+                                                (kk & 3) * 32, 16, 1024);
             if (elect_one()) mma_f16_ss(tS + NR * (gj & 1), ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
           }
           if (elect_one()) {
             mma_commit(&s_full[gj & 1]);
             mma_commit(&kv_empty[sk]);                   // K_j read
-            if (j == nb - 1) mma_commit(q_empty);        // the item's Q read for the last time
+            if (j == nb - 1) mma_commit(&q_empty[qb]);   // the item's Q read for the last time
           }
         }
         if (j > 0) {
@@ -281,9 +297,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int gb = 0;
     int it = 0;
     // Row r = (query head within the group) · seq_q + position; its last visible key.
-    int last_key[NR];
+    int last_key[RR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
+    for (int r = 0; r < RR; ++r) {
       const int sq = r % max(p.Sq, 1);
       last_key[r] = r < p.nrows ? (p.causal ? sq + p.Skv - p.Sq : p.Skv - 1) : -1;
     }
@@ -291,9 +307,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       int b, hk, kb0, kb1;
       item_coords(item, p, b, hk, kb0, kb1);
       const int nb = kb1 - kb0;
-      float m_ref[NR], l_part[NR];
+      float m_ref[RR], l_part[RR];
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
+      for (int r = 0; r < RR; ++r) {
         m_ref[r] = NEG_INF;
         l_part[r] = 0.f;
       }
@@ -301,19 +317,19 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const int key = (kb0 + j) * 128 + t;
         if (!wait_bar(&s_full[gb & 1], (uint32_t)((gb >> 1) & 1), g, 61, gb)) ok = false;
         tc_fence_after();
-        uint32_t sv[NR];
-        tmem_ld_nr<NR>(tS + lane_off + NR * (gb & 1), sv);
+        uint32_t sv[RR];
+        tmem_ld_nr<RR>(tS + lane_off + NR * (gb & 1), sv);
         tmem_wait_ld();
         tc_fence_before();
         bar_arrive(&s_empty[gb & 1]);
-        float x[NR];
+        float x[RR];
 #pragma unroll
-        for (int r = 0; r < NR; ++r)
+        for (int r = 0; r < RR; ++r)
           x[r] = key <= last_key[r] ? __uint_as_float(sv[r]) * sl : NEG_INF;
         // Block max per row: within the warp, then across the four warps.
         float* red = sRed + (gb & 1) * 4 * NR;
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
+        for (int r = 0; r < RR; ++r) {
           float v = x[r];
 #pragma unroll
           for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -321,9 +337,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         named_barrier_sync(1, 128);
         bool resc = false;
-        float alpha[NR];
+        float alpha[RR];
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
+        for (int r = 0; r < RR; ++r) {
           const float bm = fmaxf(fmaxf(red[r], red[NR + r]), fmaxf(red[2 * NR + r], red[3 * NR + r]));
           alpha[r] = 1.f;
           if (bm > m_ref[r] + 8.f) {        // also the first block that sees a key (m_ref = -inf)
@@ -338,12 +354,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           // Oᵀ holds PV up to block j-1: let it finish, then rescale its columns.
           if (!wait_bar(&p_empty[(gb - 1) & 1], (uint32_t)(((gb - 1) >> 1) & 1), g, 62, gb)) ok = false;
           tc_fence_after();
-          uint32_t o[NR];
-          tmem_ld_nr<NR>(tO + lane_off, o);
+          uint32_t o[RR];
+          tmem_ld_nr<RR>(tO + lane_off, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int r = 0; r < NR; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
-          tmem_st_nr<NR>(tO + lane_off, o);
+          for (int r = 0; r < RR; ++r) o[r] = __float_as_uint(__uint_as_float(o[r]) * alpha[r]);
+          tmem_st_nr<RR>(tO + lane_off, o);
           tmem_wait_st();
         }
         // Pᵀ of this block into buffer gb & 1 once the PV of block gb - 2 has read it.
@@ -351,7 +367,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         uint8_t* pb = sP + (gb & 1) * Cfg::kPBytes + (t >> 6) * NR * 128;
         const int kin = t & 63;            // key within the 64-key chunk
 #pragma unroll
-        for (int r = 0; r < NR; ++r) {
+        for (int r = 0; r < RR; ++r) {
           const float pr = (m_ref[r] == NEG_INF) ? 0.f : fast_exp2(x[r] - m_ref[r]);
           l_part[r] = l_part[r] * alpha[r] + pr;
           // K-major, 128-byte swizzle: 16-byte unit (kin / 8) of row r moves to (kin / 8) ^ (r % 8).
@@ -366,13 +382,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       // ---------------- epilogue of the item ----------------
       if (nb > 0 && !wait_bar(o_full, (uint32_t)(it & 1), g, 64, item)) ok = false;
       tc_fence_after();
-      uint32_t o[NR];
+      uint32_t o[RR];
       if (nb > 0) {
-        tmem_ld_nr<NR>(tO + lane_off, o);
+        tmem_ld_nr<RR>(tO + lane_off, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int r = 0; r < NR; ++r) o[r] = 0u;
+        for (int r = 0; r < RR; ++r) o[r] = 0u;
       }
       tc_fence_before();
       bar_arrive(o_empty);
@@ -380,7 +396,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       float* red = sRed;      // both halves are free: the last block's barrier has passed
       named_barrier_sync(1, 128);
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
+      for (int r = 0; r < RR; ++r) {
         float v = l_part[r];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -388,7 +404,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
       named_barrier_sync(1, 128);
 #pragma unroll
-      for (int r = 0; r < NR; ++r) {
+      for (int r = 0; r < RR; ++r) {
         if (r >= p.nrows) continue;
         const float l = (red[r] + red[NR + r]) + (red[2 * NR + r] + red[3 * NR + r]);
         const int hq = hk * p.group + r / p.Sq;
@@ -505,10 +521,10 @@ __global__ void __launch_bounds__(kDecD) attn_decode_combine_kernel(const DecPar
         den > 0.f ? (m + __log2f(den)) * 0.69314718055994530942f : -INFINITY;
 }
 
-template <int NR, bool BF16>
+template <int NR, int RR, bool BF16>
 int launch_decode(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                   const DecParams& p, int ctas, cudaStream_t stream) {
-  auto kern = attn_decode_kernel<NR, BF16>;
+  auto kern = attn_decode_kernel<NR, RR, BF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        DecCfg<NR>::kSmem);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_attention_fwd", "cudaFuncSetAttribute (decode)");
@@ -559,6 +575,12 @@ void attn_decode_plan(const lvb_attn_desc* d, int sm_count, int* nsplit, int* bp
     const double eff = (double)items / (double)(rounds * c);
     if (eff > best_eff + 1e-9) { best_eff = eff; best_ns = real_ns; }
   }
+  // LVB_DECODE_SPLITS=n forces the split count (tuning).
+  static const int forced = [] {
+    const char* e = std::getenv("LVB_DECODE_SPLITS");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced > 0) best_ns = std::min<long long>(forced, nkb);
   best_ns = std::min<long long>(best_ns, kMaxSplits);
   const int b = (int)((nkb + best_ns - 1) / best_ns);
   *nsplit = (int)((nkb + b - 1) / b);
@@ -623,12 +645,15 @@ int attn_decode_launch(const lvb_attn_desc* d, const long long qs[3], const long
   }
   const bool bf16 = d->dtype == LVB_BF16;
   int st;
-  if (NR == 16)
-    st = bf16 ? launch_decode<16, true>(tq, tk, tv, p, ctas, stream)
-              : launch_decode<16, false>(tq, tk, tv, p, ctas, stream);
+  if (nrows <= 8)
+    st = bf16 ? launch_decode<16, 8, true>(tq, tk, tv, p, ctas, stream)
+              : launch_decode<16, 8, false>(tq, tk, tv, p, ctas, stream);
+  else if (NR == 16)
+    st = bf16 ? launch_decode<16, 16, true>(tq, tk, tv, p, ctas, stream)
+              : launch_decode<16, 16, false>(tq, tk, tv, p, ctas, stream);
   else
-    st = bf16 ? launch_decode<32, true>(tq, tk, tv, p, ctas, stream)
-              : launch_decode<32, false>(tq, tk, tv, p, ctas, stream);
+    st = bf16 ? launch_decode<32, 32, true>(tq, tk, tv, p, ctas, stream)
+              : launch_decode<32, 32, false>(tq, tk, tv, p, ctas, stream);
   if (ws) {
     cudaError_t e = cudaFreeAsync(ws, stream);
     if (st == LVB_OK && e != cudaSuccess) return fail_cuda(e, op, "decode workspace free");
