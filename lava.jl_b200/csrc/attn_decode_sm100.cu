@@ -75,14 +75,18 @@ __device__ __forceinline__ void dec_drain(uint64_t* bar, uint32_t parity, uint64
 
 template <int NR>
 __device__ __forceinline__ void tmem_ld_nr(uint32_t taddr, uint32_t (&r)[NR]) {
-  if constexpr (NR == 8) tmem_ld8(taddr, r);
+  if constexpr (NR == 1) tmem_ld1(taddr, r);
+  else if constexpr (NR == 4) tmem_ld4(taddr, r);
+  else if constexpr (NR == 8) tmem_ld8(taddr, r);
   else if constexpr (NR == 16) tmem_ld16(taddr, r);
   else tmem_ld32(taddr, r);
 }
 
 template <int NR>
 __device__ __forceinline__ void tmem_st_nr(uint32_t taddr, uint32_t (&r)[NR]) {
-  if constexpr (NR == 8) tmem_st8(taddr, r);
+  if constexpr (NR == 1) tmem_st1(taddr, r);
+  else if constexpr (NR == 4) tmem_st4(taddr, r);
+  else if constexpr (NR == 8) tmem_st8(taddr, r);
   else if constexpr (NR == 16) tmem_st16(taddr, r);
   else tmem_st32(taddr, r);
 }
@@ -99,8 +103,8 @@ __device__ __forceinline__ void item_coords(int item, const DecParams& p, int& b
 }
 
 // NR: the N of the products (16 or 32, the tensor core's minimum is 16 for 128 rows); RR <= NR:
-// the rows the softmax works on (8 when the group has at most 8 query rows: the other
-// columns of Sᵀ, Pᵀ and Oᵀ are computed but never read).
+// the rows the softmax works on (1, 4, 8, 16 or 32, the smallest that holds the query rows:
+// the other columns of Sᵀ, Pᵀ and Oᵀ are computed but never read).
 template <int NR, int RR, bool BF16>
 __global__ void __launch_bounds__(kDecThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -645,7 +649,13 @@ int attn_decode_launch(const lvb_attn_desc* d, const long long qs[3], const long
   }
   const bool bf16 = d->dtype == LVB_BF16;
   int st;
-  if (nrows <= 8)
+  if (nrows == 1)
+    st = bf16 ? launch_decode<16, 1, true>(tq, tk, tv, p, ctas, stream)
+              : launch_decode<16, 1, false>(tq, tk, tv, p, ctas, stream);
+  else if (nrows <= 4)
+    st = bf16 ? launch_decode<16, 4, true>(tq, tk, tv, p, ctas, stream)
+              : launch_decode<16, 4, false>(tq, tk, tv, p, ctas, stream);
+  else if (nrows <= 8)
     st = bf16 ? launch_decode<16, 8, true>(tq, tk, tv, p, ctas, stream)
               : launch_decode<16, 8, false>(tq, tk, tv, p, ctas, stream);
   else if (NR == 16)
