@@ -409,7 +409,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       named_barrier_sync(1, 128);
 #pragma unroll
       for (int r = 0; r < RR; ++r) {
-        if (r >= p.nrows) continue;
+        // after a wait gave up the values are stale: keep the barriers, store nothing
+        if (r >= p.nrows || !ok) continue;
         const float l = (red[r] + red[NR + r]) + (red[2 * NR + r] + red[3 * NR + r]);
         const int hq = hk * p.group + r / p.Sq;
         const int sq = r % p.Sq;
@@ -433,7 +434,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       // The sums' slots are rewritten by the next item's first block only after barrier 1.
       named_barrier_sync(1, 128);
     }
-    (void)ok;
   }
 
   tc_fence_before();

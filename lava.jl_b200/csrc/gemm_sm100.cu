@@ -260,12 +260,11 @@ __device__ __forceinline__ uint32_t pack_out2(uint32_t a, uint32_t b) {
   }
 }
 
-// Staged store (D n-contiguous): the warp's 32 (m) × 32 (n) sub-tile goes to shared memory
-// as [m][n] — each lane's 32 values are one contiguous row of 64 (16-bit) or 128 (32-bit)
-// bytes, written as 16-byte vectors — and one TMA tensor store of the box {32 n, 32 m} at
-// (n0, m0w) writes it out. The rows are stored with the tensor map's swizzle (64B for 64-byte
-// rows: 16-byte chunk c of row r at c ^ ((r >> 1) & 3); 128B for 128-byte rows: c ^ (r & 7)),
-// so the 32 lanes' vector stores hit distinct banks. Only boxes wholly inside the matrix take
+// Staged store (D n-contiguous) of 32-bit outputs: the warp's 32 (m) × 32 (n) sub-tile goes
+// to shared memory as [m][n] — each lane's 32 values are one contiguous 128-byte row, written
+// as 16-byte vectors with the tensor map's 128B swizzle (16-byte chunk c of row r at
+// c ^ (r & 7)), so the 32 lanes' vector stores hit distinct banks — and one TMA tensor store of
+// the box {32 n, 32 m} at (n0, m0w) writes it out. Only boxes wholly inside the matrix take
 // this path (the store's clipping at the innermost edge is not exact to the element: a
 // 333-row matrix inside a 400-row buffer had rows 333.. overwritten), edge boxes use the
 // predicated direct stores. Two buffers per warp: a buffer is rewritten only after the store
@@ -273,25 +272,16 @@ __device__ __forceinline__ uint32_t pack_out2(uint32_t a, uint32_t b) {
 template <int OUT>
 __device__ __forceinline__ void store_staged(const CUtensorMap* tmD, const uint32_t (&r)[32],
                                              uint32_t sbase, uint32_t& cnt, int m0w, int n0) {
+  static_assert(OUT == OUT_F32 || OUT == OUT_I32, "16-bit outputs are staged in pairs");
   const uint32_t lane = lane_id();
   const uint32_t buf = sbase + (cnt & 1) * kStoreBufBytes;
   if (lane == 0) bulk_wait_group_read<1>();
   __syncwarp();
-  if constexpr (OUT == OUT_F16 || OUT == OUT_BF16) {
-    const uint32_t row = buf + lane * 64;
+  const uint32_t row = buf + lane * 128;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-      st_shared_v4(row + ((c ^ ((lane >> 1) & 3)) << 4), pack_out2<OUT>(r[8 * c], r[8 * c + 1]),
-                   pack_out2<OUT>(r[8 * c + 2], r[8 * c + 3]),
-                   pack_out2<OUT>(r[8 * c + 4], r[8 * c + 5]),
-                   pack_out2<OUT>(r[8 * c + 6], r[8 * c + 7]));
-  } else {
-    const uint32_t row = buf + lane * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      st_shared_v4(row + ((c ^ (lane & 7)) << 4), r[4 * c], r[4 * c + 1], r[4 * c + 2],
-                   r[4 * c + 3]);
-  }
+  for (int c = 0; c < 8; ++c)
+    st_shared_v4(row + ((c ^ (lane & 7)) << 4), r[4 * c], r[4 * c + 1], r[4 * c + 2],
+                 r[4 * c + 3]);
   fence_proxy_async_smem();  // this thread's writes -> visible to the TMA (async proxy)
   __syncwarp();
   if (lane == 0) {
