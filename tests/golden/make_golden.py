@@ -30,6 +30,9 @@ GEMMS = [
     ("gemm_bf16_f32_kodd", 17, 40, 200, "BFloat16", "Float32", 104),
     ("gemm_i8_i32", 70, 33, 160, "Int8", "Int32", 105),
     ("gemm_u8_u32", 20, 130, 96, "UInt8", "UInt32", 106),
+    # matrix-vector products (N = 1 / M = 1): the streaming kernel, dot4x8 for 8-bit
+    ("gemm_gemv_i8_i32", 300, 1, 1000, "Int8", "Int32", 108),
+    ("gemm_vecmat_f16_f32", 1, 200, 300, "Float16", "Float32", 109),
 ]
 
 
@@ -48,7 +51,14 @@ def main():
                         True, 0.125)
     np.savez_compressed(HERE / "attn_f16_gqa_causal.npz", kind="attention", Q=Q, K=K, V=V,
                         causal=True, scale=0.125, O=O64.astype(np.float32))
-    print("wrote", len(GEMMS) + 1, "fixtures")
+    # decoding: one query per sequence, a GQA group of 8 against a 700-key cache
+    Q, K, V = attention_inputs(2, 8, 1, 1, 128, "BFloat16", seed=110, Skv=700)
+    O64 = attention_ref(Q, K, V, True, 128 ** -0.5)
+    np.savez_compressed(HERE / "attn_bf16_decode_gqa.npz", kind="attention",
+                        Q=vocab.f32_to_bf16_bits(Q), K=vocab.f32_to_bf16_bits(K),
+                        V=vocab.f32_to_bf16_bits(V), causal=True, scale=128 ** -0.5,
+                        O=O64.astype(np.float32), dtype="BFloat16")
+    print("wrote", len(GEMMS) + 2, "fixtures")
 
 
 if __name__ == "__main__":

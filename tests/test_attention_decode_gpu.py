@@ -5,14 +5,27 @@ against the oracle. Tolerances are those of the flash-attention tests:
     BFloat16: max|Δ| <= 2^-8·(max|V| + max|O|) and relative Frobenius <= 1e-2
     lse (fp32) within 1e-3 absolute; rows that see no key: O = 0, lse = -inf.
 """
+from pathlib import Path
+
 import numpy as np
 import pytest
 
+from oracle import vocab
 from oracle.attention import attention_ref
 from oracle.inputs import attention_inputs
 from test_attention_gpu import check, run, tdt
 
 pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+
+
+def test_golden_fixture(lvb, torch_cuda):
+    """A GQA group of 8 decoding against a 700-key cache (bf16): the fixture's inputs and its
+    oracle output (tests/golden/make_golden.py)."""
+    z = np.load(GOLDEN / "attn_bf16_decode_gqa.npz")
+    Q, K, V = (vocab.bf16_bits_to_f32(z[k]) for k in ("Q", "K", "V"))
+    O = run(lvb, torch_cuda, Q, K, V, "BFloat16", bool(z["causal"]), float(z["scale"]))
+    check(O, z["O"].astype(np.float64), V, "BFloat16")
 
 
 @pytest.mark.parametrize("T", ["Float16", "BFloat16"])

@@ -24,6 +24,19 @@ def test_dot4x8_known_answers():
     assert vocab.dot4x8(0, 0xFFFFFFFF) == 0
 
 
+def test_int8_matvec_is_dot4x8():
+    """An int8 matrix-vector product as Lava's dot4x8 computes it — bytes packed four to a
+    word, row by row, each word pair summed exactly into Int32 (src/vocabulary/vocabulary.jl:
+    18-35) — equals the exact int64 GEMM oracle the GPU tests compare the kernel with."""
+    from oracle.inputs import gemm_inputs
+    A, Bt = gemm_inputs(37, 1, 96, "Int8", seed=5)
+    x = Bt[0]
+    words = lambda v: [int.from_bytes(v[i:i + 4].tobytes(), "little") for i in range(0, len(v), 4)]
+    xw = words(x)
+    y = [sum(vocab.dot4x8(a, b) for a, b in zip(words(row), xw)) for row in A]
+    assert np.array_equal(np.array(y, dtype=np.int64), gemm_ref(A, Bt.T, "Int32")[:, 0])
+
+
 def test_clamp_modes_and_reduce_masks():
     # src/vocabulary/tensor.jl:46-51, src/vocabulary/coopmat.jl:292-297
     assert (vocab.TENSOR_CLAMP_UNDEFINED, vocab.TENSOR_CLAMP_CONSTANT,
@@ -167,8 +180,11 @@ def test_golden_fixtures_reproduce():
                 got = vocab.f32_to_bf16_bits(got)
             assert np.array_equal(got, C), f.name
         elif kind == "attention":
-            O = attention_ref(z["Q"].astype(np.float32), z["K"].astype(np.float32),
-                              z["V"].astype(np.float32), bool(z["causal"]), float(z["scale"]))
+            Q, K, V = z["Q"], z["K"], z["V"]
+            if "dtype" in z.files and str(z["dtype"]) == "BFloat16":
+                Q, K, V = (vocab.bf16_bits_to_f32(x) for x in (Q, K, V))
+            O = attention_ref(Q.astype(np.float32), K.astype(np.float32),
+                              V.astype(np.float32), bool(z["causal"]), float(z["scale"]))
             assert np.abs(O - z["O"]).max() < 1e-6, f.name
 
 
