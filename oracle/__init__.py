@@ -23,6 +23,6 @@ pinned against:
 Modules: ``vocab`` (element-level restatement of the vocabulary), ``gemm`` (tiled coopmat
 GEMM following ``test/glsl/coopmat2_gemm_regs.comp:53-83`` plus a fast float64/int64
 matmul), ``attention`` (softmax attention by definition, blockwise online form),
-``inputs`` (the seeded generators of the benchmark configs), ``int8gemm`` (ctypes wrapper
-over ``int8_gemm.c``, the exact multi-threaded int8→int32 CPU GEMM).
+``inputs`` (the seeded generators of the benchmark configs). Integer products are exact
+(int64 accumulation).
 """
