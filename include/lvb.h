@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define LVB_ABI_VERSION 3
+#define LVB_ABI_VERSION 4
 
 typedef enum lvb_status {
   LVB_OK = 0,
@@ -278,6 +278,30 @@ int lvb_attention_fwd(const lvb_attn_desc* d, const void* Q, const void* K, cons
  * non-empty share. */
 int lvb_shard_range(int64_t total, int32_t world, int32_t rank, int64_t align, int64_t* begin,
                     int64_t* count);
+
+/* Optional all-gather of the shards over NVLink/NVSwitch, for hosts without their own
+ * collective library (Python hosts can use torch.distributed instead). One communicator per
+ * process and GPU, NCCL underneath; NCCL (libnccl.so.2) is opened at first use, and its
+ * absence is LVB_ERR_NCCL, not a load failure of this library. Lava has no counterpart: its
+ * runtime is single-device. */
+#define LVB_COMM_ID_BYTES 128
+typedef struct lvb_comm_id {
+  char bytes[LVB_COMM_ID_BYTES];
+} lvb_comm_id;
+typedef struct lvb_comm lvb_comm;
+/* A new communicator id. Made once (by rank 0); the host hands the bytes to every rank. */
+int lvb_comm_unique_id(lvb_comm_id* id);
+/* Join communicator `id` as `rank` of `nranks` on the current device; every rank must call
+ * it (it returns once all have joined). */
+int lvb_comm_init(lvb_comm** comm, const lvb_comm_id* id, int32_t nranks, int32_t rank);
+int lvb_comm_destroy(lvb_comm* comm);
+int lvb_comm_size(const lvb_comm* comm, int32_t* nranks, int32_t* rank);
+/* Enqueue on `stream`: recv[r·bytes .. (r+1)·bytes) = rank r's send[0 .. bytes) for every
+ * rank r (rank order, equal sizes: pad a short last shard). `send` may be recv's own slot
+ * (recv + rank·bytes). Every rank calls it with the same `bytes`, in the same order as its
+ * other collectives. For row shards of a row-major output (lvb_shard_range with the GEMM's
+ * 128-row alignment) the gathered bytes are the whole output. */
+int lvb_allgather(lvb_comm* comm, const void* send, void* recv, size_t bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Runtime helpers for host packages that own device buffers (Lava leaves these to its

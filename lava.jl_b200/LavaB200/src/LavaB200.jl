@@ -30,7 +30,7 @@ using Libdl
 using LinearAlgebra: Transpose, transpose
 
 export B200Backend, B200Array, gemm!, attention!, device_status, caps_raw, matrix_shapes_raw,
-       LavaB200Error, BFloat16
+       LavaB200Error, BFloat16, shard_range, comm_unique_id, Comm, allgather!
 
 const libpath = Ref{String}("")
 const libhandle = Ref{Ptr{Cvoid}}(C_NULL)
@@ -323,6 +323,86 @@ function device_count()
     n = Ref{Int32}(0)
     check(ccall(sym(:lvb_device_count), Cint, (Ptr{Int32},), n))
     return Int(n[])
+end
+
+# ---- several GPUs: shards and the optional all-gather -----------------------------------
+# Lava's runtime is single-device; the units of this path are independent (GEMM output rows
+# with B replicated, attention (batch, KV head) groups), so each process computes its share
+# on its own GPU and nothing is exchanged unless the caller wants the whole output on every
+# GPU (include/lvb.h: lvb_shard_range, lvb_comm_*, lvb_allgather).
+
+"""
+    shard_range(total, world, rank; align = 1) -> (first, count)
+
+`rank`'s contiguous share of `total` units (0-based `first`), made of whole chunks of
+`align` units; for GEMM rows use `align = 128` (one tile of rows).
+"""
+function shard_range(total::Integer, world::Integer, rank::Integer; align::Integer = 1)
+    b, n = Ref{Int64}(0), Ref{Int64}(0)
+    check(ccall(sym(:lvb_shard_range), Cint, (Int64, Int32, Int32, Int64, Ptr{Int64}, Ptr{Int64}),
+                total, world, rank, align, b, n))
+    return (Int(b[]), Int(n[]))
+end
+
+"""
+    comm_unique_id() -> Vector{UInt8}
+
+A fresh 128-byte communicator id, made on one process (rank 0) and handed to the others by
+the host's own channel (a file, MPI, a socket).
+"""
+function comm_unique_id()
+    id = zeros(UInt8, 128)
+    GC.@preserve id check(ccall(sym(:lvb_comm_unique_id), Cint, (Ptr{UInt8},), id))
+    return id
+end
+
+"""
+    Comm(id, nranks, rank)
+
+Join the communicator `id` as `rank` of `nranks` on the current device (NCCL over
+NVLink/NVSwitch underneath); every rank must construct it. Released by `close` or the GC.
+"""
+mutable struct Comm
+    handle::Ptr{Cvoid}
+    nranks::Int
+    rank::Int
+    function Comm(id::AbstractVector{UInt8}, nranks::Integer, rank::Integer)
+        length(id) == 128 || throw(ArgumentError("a communicator id has 128 bytes"))
+        buf = Vector{UInt8}(id)
+        h = Ref{Ptr{Cvoid}}(C_NULL)
+        GC.@preserve buf check(ccall(sym(:lvb_comm_init), Cint,
+                                     (Ptr{Ptr{Cvoid}}, Ptr{UInt8}, Int32, Int32),
+                                     h, buf, nranks, rank))
+        c = new(h[], Int(nranks), Int(rank))
+        finalizer(close, c)
+        return c
+    end
+end
+
+function Base.close(c::Comm)
+    if c.handle != C_NULL
+        h, c.handle = c.handle, C_NULL
+        check(ccall(sym(:lvb_comm_destroy), Cint, (Ptr{Cvoid},), h))
+    end
+    return nothing
+end
+
+"""
+    allgather!(recv, send, comm; stream = C_NULL)
+
+Enqueue on `stream`: `recv` (nranks × the bytes of `send`) receives every rank's `send` in
+rank order. Shards of equal size: pad a short last shard. With column-major Julia arrays a
+gather of row shards is a gather of the shards of Cᵀ (compute Cᵀ = BᵀAᵀ per shard, or
+shard by output columns).
+"""
+function allgather!(recv::B200Array{T}, send::B200Array{T}, comm::Comm;
+                    stream = C_NULL) where {T}
+    nb = sizeof(T) * length(send)
+    sizeof(T) * length(recv) == nb * comm.nranks ||
+        throw(DimensionMismatch("recv must hold nranks × the elements of send"))
+    check(ccall(sym(:lvb_allgather), Cint, (Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Csize_t, Ptr{Cvoid}),
+                comm.handle, pointer(send), pointer(recv), nb, stream))
+    return recv
 end
 
 end # module

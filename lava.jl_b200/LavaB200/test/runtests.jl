@@ -26,6 +26,13 @@ using LinearAlgebra
         @test err isa LavaB200Error && err.operation == "lvb_gemm"
     end
 
+    @testset "shards and communicator ids (no GPU)" begin
+        @test [shard_range(1000, 2, r; align = 128) for r in 0:1] == [(0, 512), (512, 488)]
+        id = comm_unique_id()
+        @test length(id) == 128 && id != comm_unique_id()
+        @test_throws LavaB200Error Comm(zeros(UInt8, 128), 2, 2)
+    end
+
     if LavaB200.device_count() > 0
         @testset "gemm! Float16 -> Float32 (GPU)" begin
             M, N, K = 300, 200, 136

@@ -21,7 +21,7 @@ CSRC = HERE / "csrc"
 LIBDIR = HERE / "lib"
 LIB = LIBDIR / "liblvb.so"
 SOURCES = ["abi.cu", "gemm_sm100.cu", "gemv_sm100.cu", "attn_sm100.cu", "attn_decode_sm100.cu",
-           "selftest.cu"]
+           "selftest.cu", "comm.cu"]
 HEADERS = ["sm100.cuh", "epilogue.cuh", "lvb_internal.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -62,7 +62,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
             sys.stderr.write(r.stderr)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *objs]
+    cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *objs, "-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -53,6 +53,7 @@ EXPORTS = [
     "lvb_stream_create", "lvb_stream_destroy", "lvb_stream_synchronize",
     "lvb_device_status", "lvb_set_wait_timeout_ms", "lvb_shard_range",
     "lvb_selftest_wait_timeout",
+    "lvb_comm_unique_id", "lvb_comm_init", "lvb_comm_destroy", "lvb_comm_size", "lvb_allgather",
 ]
 
 
@@ -125,6 +126,10 @@ class lvb_attn_desc(C.Structure):
                 ("v_stride", C.c_int64 * 3), ("o_stride", C.c_int64 * 3)]
 
 
+class lvb_comm_id(C.Structure):
+    _fields_ = [("bytes", C.c_char * 128)]
+
+
 def _load() -> C.CDLL:
     if not LIB_PATH.exists():
         raise ImportError(f"liblvb.so not built at {LIB_PATH}; run python lava.jl_b200/build.py")
@@ -161,6 +166,11 @@ def _load() -> C.CDLL:
         "lvb_shard_range": ([C.c_int64, C.c_int32, C.c_int32, C.c_int64, C.POINTER(C.c_int64),
                              C.POINTER(C.c_int64)], C.c_int),
         "lvb_selftest_wait_timeout": ([C.c_int32, P], C.c_int),
+        "lvb_comm_unique_id": ([C.POINTER(lvb_comm_id)], C.c_int),
+        "lvb_comm_init": ([C.POINTER(P), C.POINTER(lvb_comm_id), C.c_int32, C.c_int32], C.c_int),
+        "lvb_comm_destroy": ([P], C.c_int),
+        "lvb_comm_size": ([P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)], C.c_int),
+        "lvb_allgather": ([P, P, P, C.c_size_t, P], C.c_int),
     }
     for name, (args, res) in sig.items():
         f = getattr(lib, name)

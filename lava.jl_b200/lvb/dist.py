@@ -43,3 +43,49 @@ def allgather_rows(local, group=None):
                       device=local.device)
     dist.all_gather_into_tensor(out, local.contiguous(), group=group)
     return out
+
+
+class Comm:
+    """The C ABI's own NCCL communicator (lvb_comm_*), the all-gather a host without
+    torch.distributed uses (the Julia package binds the same calls). One per process and GPU.
+
+        uid = Comm.unique_id()            # on rank 0, then sent to the others
+        comm = Comm(uid, world, rank)     # every rank, on its current device
+        comm.allgather(send, recv)        # recv = the ranks' sends, concatenated in rank order
+    """
+
+    @staticmethod
+    def unique_id() -> bytes:
+        from . import lvb_comm_id
+        uid = lvb_comm_id()
+        check(lib.lvb_comm_unique_id(C.byref(uid)))
+        return C.string_at(C.addressof(uid), 128)
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        from . import lvb_comm_id
+        if len(uid) != 128:
+            raise ValueError("a communicator id has 128 bytes")
+        cid = lvb_comm_id()
+        C.memmove(C.addressof(cid), uid, 128)
+        h = C.c_void_p()
+        check(lib.lvb_comm_init(C.byref(h), C.byref(cid), int(nranks), int(rank)))
+        self._h = h
+        self.nranks, self.rank = int(nranks), int(rank)
+
+    def allgather(self, send, recv, stream=None) -> None:
+        """recv (a device tensor of nranks · send.nbytes bytes) <- every rank's send, in rank
+        order, enqueued on `stream` (default: torch's current stream)."""
+        import torch
+        nbytes = send.numel() * send.element_size()
+        if recv.numel() * recv.element_size() != nbytes * self.nranks:
+            raise ValueError("recv must hold nranks x send bytes")
+        if not (send.is_contiguous() and recv.is_contiguous()):
+            raise ValueError("send and recv must be contiguous")
+        s = stream if stream is not None else torch.cuda.current_stream()
+        check(lib.lvb_allgather(self._h, C.c_void_p(send.data_ptr()), C.c_void_p(recv.data_ptr()),
+                                nbytes, C.c_void_p(s.cuda_stream)))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib.lvb_comm_destroy(self._h))
+            self._h = None

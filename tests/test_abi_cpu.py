@@ -37,7 +37,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
     structs = {"lvb_matrix_shape": lvb.lvb_matrix_shape, "lvb_device_caps": lvb.lvb_device_caps,
                "lvb_gemm_desc": lvb.lvb_gemm_desc, "lvb_gemm_plan": lvb.lvb_gemm_plan,
                "lvb_attn_desc": lvb.lvb_attn_desc, "lvb_epilogue": lvb.lvb_epilogue,
-               "lvb_attn_plan": lvb.lvb_attn_plan}
+               "lvb_attn_plan": lvb.lvb_attn_plan, "lvb_comm_id": lvb.lvb_comm_id}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "lvb.h"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
@@ -59,7 +59,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
 def test_library_needs_no_libcuda_at_load(lvb):
     out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
     assert "libcuda.so" not in out
-    assert lvb.abi_version() == 3
+    assert lvb.abi_version() == 4
 
 
 def test_static_caps_answer(lvb):

@@ -93,3 +93,26 @@ def test_two_rank_shard_and_gather_gloo(lvb):
     res = sorted(q.get(timeout=5) for _ in range(2))
     for rank, ok_gemm, ok_attn, tmax in res:
         assert ok_gemm and ok_attn and tmax == 2.0
+
+
+def test_comm_host_side(lvb):
+    """The C ABI's all-gather (lvb_comm_*) without a GPU: communicator ids (128 bytes, fresh
+    each time) and the argument checks that come before any device work."""
+    import ctypes as C
+    from lvb.dist import Comm
+    try:
+        u1, u2 = Comm.unique_id(), Comm.unique_id()
+    except lvb.LavaError as e:            # no NCCL on this machine: reported, not a crash
+        assert e.status == 5
+    else:
+        assert len(u1) == len(u2) == 128 and u1 != u2
+    for nranks, rank in [(2, 2), (2, -1), (0, 0)]:
+        with pytest.raises(lvb.LavaError) as ei:
+            Comm(bytes(128), nranks, rank)
+        assert ei.value.status == 1
+    with pytest.raises(ValueError):
+        Comm(bytes(5), 1, 0)
+    assert lvb.lib.lvb_allgather(None, None, None, 16, None) == 1
+    assert lvb.lib.lvb_comm_destroy(None) == 0
+    n, r = C.c_int32(), C.c_int32()
+    assert lvb.lib.lvb_comm_size(None, C.byref(n), C.byref(r)) == 1
