@@ -1,7 +1,7 @@
 """Seeded synthetic inputs of the benchmark configurations — TEST INFRASTRUCTURE.
 
 Generator: ``numpy.random.Generator(PCG64(seed))`` (Julia's RNG stream cannot be
-reproduced without Julia; parity is always judged on identical input bytes). Draw order is
+reproduced without Julia; parity is always checked on identical input bytes). Draw order is
 fixed: A first, then B, each in its STORAGE order — A (M,K) row-major, B (K,N) column-major
 drawn as its (N,K) storage array — so the same seed gives the same bytes everywhere.
 
