@@ -374,7 +374,12 @@ mutable struct Comm
                                      (Ptr{Ptr{Cvoid}}, Ptr{UInt8}, Int32, Int32),
                                      h, buf, nranks, rank))
         c = new(h[], Int(nranks), Int(rank))
-        finalizer(close, c)
+        finalizer(c) do x          # no exceptions from a finalizer: the status is dropped
+            if x.handle != C_NULL
+                ccall(sym(:lvb_comm_destroy), Cint, (Ptr{Cvoid},), x.handle)
+                x.handle = C_NULL
+            end
+        end
         return c
     end
 end
