@@ -491,10 +491,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int e = 0; e < 16; ++e)
           pk[e] = pack2<BF16>(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
         if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+          uint8_t* dst = orow + c * 64;
+          if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+            // 32-byte stores: each lane's store fills a whole 32-byte sector of its row.
+            st_global_v8(dst, &pk[0]);
+            st_global_v8(dst + 32, &pk[8]);
+          } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dst[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+            for (int e = 0; e < 4; ++e)
+              reinterpret_cast<uint4*>(dst)[e] =
+                  make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          }
         }
       }
       tc_fence_before();

@@ -99,6 +99,25 @@ def test_strided_views(lvb, torch_cuda):
     check(dO.float().cpu().numpy(), ref, V, "Float16")
 
 
+
+def test_output_rows_16_byte_aligned(lvb, torch_cuda):
+    """Output rows 272 bytes apart from a base 16 bytes past a 32-byte boundary: rows alternate
+    between the epilogue's 32-byte stores and its 16-byte stores; the padding between rows
+    stays untouched."""
+    torch = torch_cuda
+    Q, K, V = attention_inputs(1, 4, 2, 300, 128, "Float16", seed=95)
+    dQ, dK, dV = (torch.from_numpy(x).cuda() for x in (Q, K, V))
+    buf = torch.full((4 * 300 * 136 + 8,), 7.0, dtype=torch.float16, device="cuda")
+    rows = buf[8:].view(1, 4, 300, 136)
+    assert rows.data_ptr() % 32 == 16
+    dO = rows[..., :128]
+    lvb.attention(dO, dQ, dK, dV, causal=True)
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    ref = attention_ref(Q, K, V, True, 128 ** -0.5)
+    check(dO.float().cpu().numpy(), ref, V, "Float16")
+    assert bool((rows[..., 128:] == 7).all()) and bool((buf[:8] == 7).all())
+
 def _full_config(lvb, torch, name, units):
     cfg = ATTN_CONFIGS[name]
     T = cfg["dtype"]
