@@ -431,6 +431,16 @@ __device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
+// The same arrive without release semantics, for a hand-off whose only hazard is tcgen05
+// state: TMEM columns this thread read with tcgen05.ld, completed by tcgen05.wait::ld and
+// ordered before the arrive by tcgen05.fence::before_thread_sync; the waiter reads no memory
+// this thread wrote. A release at cluster scope would first wait for all of the thread's
+// earlier memory operations (an epilogue's shared-memory staging and stores) to become
+// visible across the cluster: measured ~1,100 clk per tile in the GEMM epilogue.
+__device__ __forceinline__ void bar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
 // 2-D tiled load into this CTA's shared memory whose completion bytes are signalled on an
 // mbarrier of either CTA of the pair (`bar_cluster` is a shared::cluster address).
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, int32_t c0,
