@@ -15,13 +15,15 @@
 //     MN-major in place (Lava's transposing tensor view); a CTA owns a 128 × BN output tile;
 //   * warp 0 lane 0: TMA producer. Streams 128×128-byte A and BN×128-byte B boxes
 //     (128B swizzle, zero fill past the edges) into a STAGES-deep mbarrier ring;
-//   * warp 1 lane 0: MMA issuer. Four tcgen05.mma (128×BN×16 f16 / ×32 i8) per stage into
-//     one of two TMEM accumulators, tcgen05.commit frees the stage;
+//   * warp 1: MMA issuer (the converged warp waits, an elected lane issues). Four
+//     tcgen05.mma (128×BN×16 f16 / ×32 i8) per stage into one of two TMEM accumulators,
+//     tcgen05.commit frees the stage;
 //   * warp 2: allocates / frees TMEM (2·BN columns);
 //   * warps 4-7: epilogue. tcgen05.ld 32 columns at a time; lane = output row, so each
-//     store of one column by a warp writes 32 consecutive m (coalesced, D is m-contiguous);
-//     the accumulator is handed back as soon as it has been read, so the next tile's MMAs
-//     overlap this tile's stores.
+//     store of one column by a warp writes 32 consecutive m (coalesced, D is m-contiguous),
+//     or, with D n-contiguous, 32 × 128-byte boxes staged in shared memory go out as TMA
+//     tensor stores; the accumulator is handed back as soon as it has been read, so the
+//     next tile's MMAs overlap this tile's stores.
 //   * persistent grid (one CTA per SM), tiles visited in groups of GROUP_M row-tiles so the
 //     ~148 tiles in flight share A rows and B columns in L2.
 #include <algorithm>
