@@ -245,3 +245,20 @@ def test_config3_int8_8192_exact_sampled_rows(lvb, torch_cuda):
     # a checksum of every row: sum_n C[m,n] == A[m,:] · (sum_n B[:,n])
     colsum = Bt.astype(np.int64).sum(axis=0)            # (K,)
     assert np.array_equal(C.astype(np.int64).sum(axis=1), A.astype(np.int64) @ colsum)
+
+
+@pytest.mark.parametrize("c_rowmajor", [False, True])
+def test_small_k_many_tiles_exact(lvb, torch_cuda, c_rowmajor):
+    """8192 x 8192 x 32 int8: 1,024 output tiles, ~14 per CTA pair, whose epilogue (the whole
+    run time at this K) hands each accumulator back to the MMA warp as soon as it has been
+    read. Every element is compared exactly, so an accumulator overwritten before it was
+    read would show."""
+    torch = torch_cuda
+    M = N = 8192
+    K = 32
+    A, Bt = gemm_inputs(M, N, K, "Int8", seed=31)
+    C = run(lvb, torch, A, Bt, "Int8", "Int32", c_rowmajor=c_rowmajor)
+    B64 = Bt.T.astype(np.float64)
+    for r0 in range(0, M, 1024):     # float64 BLAS is exact: partial sums below 2^53
+        ref = (A[r0:r0 + 1024].astype(np.float64) @ B64).astype(np.int64)
+        assert np.array_equal(C[r0:r0 + 1024].astype(np.int64), ref), r0
