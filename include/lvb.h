@@ -205,7 +205,7 @@ int lvb_gemm_ex(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, co
 
 /* lvb_gemm for callers that must not allocate device memory while they run a GEMM (a host
  * runtime that owns all device memory through its own pool, a serving loop that forbids
- * allocation after warm-up, work enqueued during stream capture). No counterpart in the
+ * allocation after warm-up). No counterpart in the
  * reference: Lava has no host GEMM entry point at all; this is a second form of lvb_gemm.
  * Same arguments, semantics and results as lvb_gemm; it calls no cudaMalloc, cudaFree,
  * cudaMallocAsync or other device allocator. Its scratch — the device status word and the

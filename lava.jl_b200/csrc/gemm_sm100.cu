@@ -1039,12 +1039,10 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
 //
 // Some hosts may not allocate device memory at the moment they run a GEMM: a runtime that
 // owns every byte of device memory through its own pool and forbids allocations behind its
-// back, a serving loop that must not allocate after warm-up, or code that enqueues work
-// while a stream is being captured (cudaMalloc / cudaMallocAsync are not allowed there in
-// the way lvb_gemm uses them). For them the scratch this GEMM needs lives in one
-// file-scope device array instead: the device status word at its head, and the workspace
-// that operands TMA cannot address (base or leading dimension not a 16-byte multiple) are
-// repacked into. Every GPU that loads the library keeps this array until the process exits.
+// back, or a serving loop that must not allocate after warm-up. For them the scratch this
+// GEMM needs lives in one file-scope device array instead: the device status word at its
+// head, and the workspace that operands TMA cannot address (base or leading dimension not a
+// 16-byte multiple) are repacked into. Every GPU that loads the library keeps this array until the process exits.
 // ----------------------------------------------------------------------------------------
 constexpr size_t kNoAllocHeadBytes = 256;                   // DevStatus, padded
 constexpr size_t kNoAllocWorkspaceBytes = 16ull << 20;      // repack workspace: 16 MiB

@@ -1,7 +1,7 @@
 """GPU tier: lvb_gemm_noalloc, the GEMM entry point for callers that must not allocate
 device memory while they run it (a runtime that owns all device memory through its own
-pool, a serving loop that forbids allocation after warm-up, work enqueued during stream
-capture). Its scratch is one static device array shared by every call.
+pool, a serving loop that forbids allocation after warm-up). Its scratch is one static
+device array shared by every call.
 
 Each case calls it through the C ABI twice in a row and compares the result with what
 lvb_gemm gives for the same operands, within the GEMM tests' tolerance (the two share the
