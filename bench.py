@@ -11,6 +11,15 @@ collective on the data path). Rank 0 prints one JSON line: whole-job TFLOP/s ove
 of the ranks' device times, plus roofline, end-to-end (host buffers, copies inside the
 timed region), CPU baseline and SM clocks sampled during the timed region.
 
+The same line carries the rest of the metric, each timed in its own region with its own
+roofline and clock record (skipped with --no-extras):
+  * "attention": C4 (fp16, B4 H32 S4096 causal) and C5 (bf16 GQA, B8 Hq64 Hkv8 S16384
+    causal) — one problem each, its (batch, KV head) units sharded over the N ranks (strong
+    scaling; at N = 1 the whole problem on one GPU);
+  * "split": C3 (int8 8192^3) with the rows of A and C sharded in 128-row blocks over the
+    N ranks (strong scaling), and at N > 1 the NCCL all-gather of C timed apart;
+  * "cublas": torch.matmul on the headline GEMM's operands, a library figure beside ours.
+
 ``--impl reference`` times the reference's CPU path stand-in (the oracle port: host
 float32 BLAS, or exact float64 BLAS for int8, or blockwise float32 attention) on the host
 cores — Lava's own path (Lava→SPIR-V on lavapipe, host Julia BLAS) needs Julia and a
@@ -261,6 +270,13 @@ def cpu_baseline(w, budget_s: float = 12.0):
 
 
 def run_reference(args, w):
+    # Every host core, whatever the launcher set: torchrun exports OMP_NUM_THREADS=1, which
+    # would leave the host BLAS on one thread (and shrink the time-sized sample) at N > 1.
+    try:
+        from threadpoolctl import threadpool_limits
+        limits = threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+    except Exception:  # noqa: BLE001
+        limits = None
     step, units, sample = cpu_step_factory(w, target_s=1.0)
     for _ in range(args.warmup):
         step()
@@ -269,6 +285,9 @@ def run_reference(args, w):
         t0 = time.perf_counter()
         step()
         times.append(time.perf_counter() - t0)
+    threads = blas_threads()
+    if limits is not None:
+        limits.restore_original_limits()
     tot = sum(times)
     value = units * len(times) / tot / 1e12
     unit = "TOPS" if w["ab"] == "Int8" else "TFLOP/s"
@@ -277,8 +296,8 @@ def run_reference(args, w):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": tot / len(times) * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": w["dtype"], "data": "synthetic (seeded)",
-        "config": config_of(w, args.gpus, reference=True),
-        "cpu_baseline": {"value": value, "unit": unit, "cores": blas_threads(), "kind": "port",
+        "config": config_of(w, args.gpus), "device": "host CPU",
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port",
                          "sample": sample, "host_cpus": os.cpu_count()},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": ("Lava's own path (Julia -> SPIR-V on lavapipe, host Julia BLAS) is unavailable "
@@ -287,7 +306,7 @@ def run_reference(args, w):
     print(json.dumps(line), flush=True)
 
 
-def config_of(w, n, reference=False):
+def config_of(w, n):
     c = {"workload": f"{w['cfg']} " + (
         f"{w['ab']} GEMM M={w['M']} N={w['N']} K={w['K']} per GPU, {w['out']} C, "
         f"A {'row' if w.get('a_rowmajor', True) else 'column'}-major, "
@@ -299,8 +318,6 @@ def config_of(w, n, reference=False):
     c["parallelism"] = (f"row-shard x{n} (independent shards, no collective)" if w["kind"] == "gemm"
                         else f"(batch, kv-head) shard x{n}") if n > 1 else "single GPU"
     c["l2"] = "inputs larger than L2 (126 MB): working set re-read every step from HBM"
-    if reference:
-        c["device"] = "host CPU"
     return c
 
 
@@ -425,6 +442,179 @@ def run_e2e(torch, compute, ins, outs, steps):
     t1.record(s_out)
     t1.synchronize()
     return t0.elapsed_time(t1) / steps
+
+
+# ----------------------------------------------------------------------------------------
+# The rest of the metric on the same line: attention (C4, C5) and the north star's split
+# problem (C3 row-sharded over the ranks, one problem in total), each timed on its own
+# ----------------------------------------------------------------------------------------
+def timed_region(torch, step, steps, warmup, stream, local, sync, max_over_ranks):
+    """Warm-up, then `steps` calls between CUDA events on `stream` with SM clocks sampled;
+    returns (this rank's ms per step, max over ranks, clock record)."""
+    for _ in range(warmup):
+        step()
+    sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    clocks = sampler.stop()
+    ms_local = e0.elapsed_time(e1) / steps
+    sync()
+    return ms_local, max_over_ranks(ms_local), clocks
+
+
+def tensor_roofline(flop_local, ms_local, steps, peaks, src, scale=1.0):
+    """Roofline of one timed region against the measured bf16 GEMM (x2 for int8): the
+    sustained figure for regions of a second or more, the burst figure otherwise."""
+    timed_s = ms_local * steps / 1e3
+    kind = "sustained" if timed_s >= 1.0 else "burst"
+    burst = peaks["bf16_tflops"] * scale
+    peak = (peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]) * scale
+            if kind == "sustained" else burst)
+    achieved = flop_local / (ms_local * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": achieved, "peak": peak,
+            "unit": "TOPS" if scale != 1.0 else "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": kind, "frac_of_burst": achieved / burst, "timed_region_s": timed_s,
+            "peak_source": f"{src} bf16_tflops{'_sustained' if kind == 'sustained' else ''}"
+                           f"{' x2 (int8 dense rate)' if scale != 1.0 else ''}"}
+
+
+def attention_shard(torch, lvb, name, world, rank):
+    """This rank's share of attention config `name`, sharded by (batch, KV head) units (a
+    unit carries its group of query heads: no K/V is duplicated): n units laid out as a batch
+    of n with Hkv = 1, Hq = group — the same work items as the whole problem's."""
+    from lvb.dist import attention_units
+    w = {"C4": WORKLOADS["attn_f16"], "C5": WORKLOADS["attn_bf16"]}[name]
+    Bn, Hq, Hkv, S, D = w["B"], w["Hq"], w["Hkv"], w["S"], w["D"]
+    g = Hq // Hkv
+    units = attention_units(Bn, Hkv, world, rank)
+    n = len(units)
+    tdt = torch.float16 if w["ab"] == "Float16" else torch.bfloat16
+    gen = torch.Generator(device="cuda").manual_seed(w["seed"] * 1000 + rank)
+    Q = torch.randn((n, g, S, D), generator=gen, device="cuda").to(tdt)
+    K = torch.randn((n, 1, S, D), generator=gen, device="cuda").to(tdt)
+    V = torch.randn((n, 1, S, D), generator=gen, device="cuda").to(tdt)
+    O = torch.empty_like(Q)
+    flop_local = 4.0 * n * g * S * S * D / 2
+    flop_total = work_units(w)
+    plan = lvb.attention_plan(n, g, 1, S, S, D, lvb.F16 if w["ab"] == "Float16" else lvb.BF16,
+                              True, sm_count=torch.cuda.get_device_properties(0).multi_processor_count)
+
+    def step():
+        lvb.attention(O, Q, K, V, causal=True)
+    return w, step, flop_local, flop_total, plan.launches, (Q, K, V, O), n
+
+
+def measure_extras(args, torch, lvb, world, rank, local, stream, sync, max_over_ranks):
+    """Secondary keys of the bench line (see the module docstring)."""
+    peaks, src = measured_peaks()
+    out = {}
+    # ---- attention: C4 and C5, the one problem sharded by (batch, KV head) over the ranks ----
+    att = {}
+    for name in ("C4", "C5"):
+        w, step, fl, ft, launches, keep, n = attention_shard(torch, lvb, name, world, rank)
+        steps = args.steps if name == "C4" else max(3, min(args.steps, 20))
+        ms_l, ms, clocks = timed_region(torch, step, steps, args.warmup, stream, local, sync,
+                                        max_over_ranks)
+        st = lvb.device_status()
+        assert st[0] == 0, f"device status {st} after attention {name}"
+        att[name] = {
+            "workload": config_of(w, 1)["workload"].replace(" per GPU", ""),
+            "value": ft / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "steps": steps, "units_per_rank": n, "flop_per_step": ft,
+            "parallelism": (f"(batch, kv-head) units sharded over {world} ranks, one problem"
+                            if world > 1 else "single GPU"),
+            "scaling": "strong" if world > 1 else None,
+            "roofline": tensor_roofline(fl, ms_l, steps, peaks, src),
+            "clocks": clocks, "gpu_launches": steps * launches}
+        del keep
+        torch.cuda.empty_cache()
+    out["attention"] = att
+    # ---- C3 int8 8192^3 row-sharded (128-row blocks) over the ranks, then the all-gather ----
+    from lvb.dist import gemm_rows, allgather_rows
+    w = WORKLOADS["gemm_i8"]
+    M, N, K = w["M"], w["N"], w["K"]
+    r0, rn = gemm_rows(M, world, rank)
+    gen = torch.Generator(device="cuda").manual_seed(w["seed"] * 1000 + rank)
+    A = torch.randint(-128, 128, (max(rn, 1), K), generator=gen, device="cuda",
+                      dtype=torch.int16).to(torch.int8)[:rn]
+    g2 = torch.Generator(device="cuda").manual_seed(w["seed"])   # B replicated: same on all
+    Bm = torch.randint(-128, 128, (N, K), generator=g2, device="cuda", dtype=torch.int16).to(torch.int8)
+    Cm = torch.empty((rn, N), dtype=torch.int32, device="cuda")
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    plan = lvb.gemm_plan(max(rn, 1), N, K, lvb.I8, lvb.I32, c_rowmajor=True, sm_count=sms)
+
+    def gstep():
+        if rn:
+            lvb.gemm(Cm, A, Bm.t())
+    ms_l, ms, clocks = timed_region(torch, gstep, args.steps, args.warmup, stream, local, sync,
+                                    max_over_ranks)
+    st = lvb.device_status()
+    assert st[0] == 0, f"device status {st} after the split GEMM"
+    split = {
+        "workload": f"C3 Int8 GEMM M={M} N={N} K={K} Int32 C (row-major), rows of A and C "
+                    f"sharded in 128-row blocks over the ranks ({rn} rows on rank {rank}), "
+                    "B replicated",
+        "value": 2.0 * M * N * K / (ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms,
+        "steps": args.steps, "rows_per_rank": rn, "scaling": "strong" if world > 1 else None,
+        "tiles_per_rank": plan.tiles, "ctas": plan.ctas, "cta_pair": plan.cta_pair,
+        "roofline": tensor_roofline(2.0 * rn * N * K, ms_l, args.steps, peaks, src, scale=2.0),
+        "clocks": clocks, "gpu_launches": args.steps * plan.launches, "allgather": None}
+    if world > 1:
+        for _ in range(2):
+            full = allgather_rows(Cm, total=M)
+        sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            full = allgather_rows(Cm, total=M)
+        e1.record(stream)
+        e1.synchronize()
+        ag_ms = max_over_ranks(e0.elapsed_time(e1) / reps)
+        nbytes = full.numel() * full.element_size()
+        split["allgather"] = {
+            "ms": ag_ms, "bytes": nbytes,
+            "busbw_GBs": nbytes * (world - 1) / world / (ag_ms * 1e-3) / 1e9,
+            "algbw_GBs": nbytes / (ag_ms * 1e-3) / 1e9,
+            "how": "torch.distributed all_gather_into_tensor of the int32 C row blocks (NCCL "
+                   "over NVLink/NVSwitch), timed apart from the GEMM"}
+        split["value_with_allgather"] = 2.0 * M * N * K / ((ms + ag_ms) * 1e-3) / 1e12
+        del full
+        sync()
+    out["split"] = split
+    del A, Bm, Cm
+    torch.cuda.empty_cache()
+    return out
+
+
+def cublas_sanity(torch, w, ins, steps, warmup, stream):
+    """torch.matmul (cuBLAS) on the headline GEMM's operands in the same kind of timed
+    region: a library figure beside the kernel's, not part of `value`."""
+    if w["kind"] != "gemm" or w.get("epilogue") or w["ab"] == "Int8":
+        return None
+    A, B = ins[0], ins[1]
+    a = A if w.get("a_rowmajor", True) else A.t()
+    b = B.t() if not w.get("b_rowmajor", False) else B
+    out = torch.empty((a.shape[0], b.shape[1]), dtype=a.dtype, device="cuda")
+    for _ in range(warmup):
+        torch.matmul(a, b, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        torch.matmul(a, b, out=out)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del out
+    return {"value": work_units(w) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "steps": steps, "how": "torch.matmul (cuBLAS) on the same operands, same steps"}
 
 
 def run_gpu(args, w):
@@ -561,6 +751,15 @@ def run_gpu(args, w):
                    "how": "lvb_gemm without epilogue, then torch elementwise "
                           f"{w['epilogue']}(C + bias + R) as a second pass over C"}
 
+    cublas = None
+    if not args.no_extras:
+        cublas = cublas_sanity(torch, w, ins, args.steps, args.warmup, stream)
+    extras = None
+    if not args.no_extras and args.workload == "gemm_f16":
+        torch.cuda.empty_cache()
+        extras = measure_extras(args, torch, lvb, world, rank, local, stream, barrier,
+                                max_over_ranks)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w)
@@ -594,8 +793,9 @@ def run_gpu(args, w):
             "impl": "lvb", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": w["dtype"], "data": "synthetic: seeded torch RNG, shapes/distributions of "
-            f"BASELINE {w['cfg']}",
+            "dtype": w["dtype"], "data": "synthetic: torch.Generator on the GPU (seed = the "
+            "config's seed x 1000 + rank), not the configs' numpy PCG64 streams (the parity "
+            f"tests use those); shapes and distributions of BASELINE {w['cfg']}",
             "config": config_of(w, world),
             "roofline": ({"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                           "frac": gbs / hbm_peak, "traffic": traffic,
@@ -626,6 +826,10 @@ def run_gpu(args, w):
         }
         if unfused:
             line["unfused_comparison"] = unfused
+        if cublas:
+            line["cublas"] = cublas
+        if extras:
+            line.update(extras)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -644,6 +848,8 @@ def main():
                     help="also time an NCCL all-gather of the outputs (N > 1), reported apart")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the end-to-end leg (used for short profiling runs)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the attention / split-GEMM / cuBLAS keys of the default line")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.steps is None:

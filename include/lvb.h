@@ -209,18 +209,31 @@ int lvb_gemm_ex(const lvb_gemm_desc* d, const lvb_epilogue* e, const void* A, co
  * reference: Lava has no host GEMM entry point at all; this is a second form of lvb_gemm.
  * Same arguments, semantics and results as lvb_gemm; it calls no cudaMalloc, cudaFree,
  * cudaMallocAsync or other device allocator. Its scratch — the device status word and the
- * workspace for operands whose base or leading dimension is not a 16-byte multiple — is one
- * static device array of 16 MiB + 256 bytes that every GPU loading the library keeps until
- * the process exits. Operands needing more than 16 MiB of repack workspace are refused with
- * LVB_ERR_UNSUPPORTED (aligned operands need none, at any size). The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) with that device current; make
- * that first call before any stream capture. All calls share the one array and it keeps the
- * last call's contents (the status word is cleared at the start of each call): calls that
- * can overlap on the GPU (different streams, or different host threads) race on it and must
- * be ordered by the caller. A wait that runs out is recorded in that shared word, not in the
- * word lvb_device_status reads. */
+ * workspace for operands that must be copied first — is one static device array of
+ * 16 MiB + 256 bytes that every GPU loading the library keeps until the process exits.
+ * Operands needing more than 16 MiB of copies are refused with LVB_ERR_UNSUPPORTED. An operand
+ * is copied when its base or leading dimension is not a 16-byte multiple, and an 8-bit operand
+ * stored MN-contiguous (Int8/UInt8 A column-major or B row-major) is copied K-major at any
+ * alignment; other operands need no copy, at any size. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current, which also
+ * loads this part of the library onto the device when CUDA loads modules lazily (the array
+ * is placed on the device then); make that first call before any stream capture. The address
+ * is looked up again when the device's context has been replaced (cudaDeviceReset). All
+ * calls share the one array and it keeps the last call's contents (the status word is cleared
+ * at the start of each call): calls that can overlap on the GPU (different streams, or
+ * different host threads) race on it and must be ordered by the caller. A wait that runs out
+ * is recorded in that shared word, which lvb_gemm_noalloc_status reads (not the word
+ * lvb_device_status reads). */
 int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const void* B, void* C,
                      void* stream);
+/* Synchronise `stream`, then read and clear lvb_gemm_noalloc's status word on the current
+ * device: *code is LVB_OK or LVB_ERR_TIMEOUT (a bounded wait inside the last noalloc call ran
+ * out and C is incomplete), *where the wait site, *block the first CTA that gave up. Allocates
+ * nothing. No counterpart in the reference (see lvb_gemm_noalloc). */
+int lvb_gemm_noalloc_status(void* stream, int32_t* code, int32_t* where, int32_t* block);
+/* Failure-path self-test of that word: lvb_selftest_wait_timeout recording into
+ * lvb_gemm_noalloc's status word instead of lvb_device_status's. Allocates nothing. */
+int lvb_gemm_noalloc_selftest_wait_timeout(int32_t timeout_ms, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Flash-attention forward: O = softmax(scale·Q·Kᵀ + mask)·V per (batch, query head), fp32

@@ -28,6 +28,10 @@ module LavaB200
 
 using Libdl
 using LinearAlgebra: Transpose, transpose
+# Lava's backend-form queries (`matrix_shapes(backend)`, `supports(backend, s)`,
+# `bestshape(backend, ab, acc)`, src/vocabulary/caps.jl:158-169, matrix.jl:138-141) dispatch
+# on `backend::KI.Backend` and call `caps(backend)`; B200Backend subtypes it so they resolve.
+import KernelInterface as KI
 
 export B200Backend, B200Array, gemm!, attention!, device_status, caps_raw, matrix_shapes_raw,
        LavaB200Error, BFloat16, shard_range, comm_unique_id, Comm, allgather!
@@ -129,8 +133,13 @@ struct AttnDesc
 end
 
 # ---- capabilities ----------------------------------------------------------------------
-"""The backend type a kernel library dispatches on to reach this library."""
-struct B200Backend
+"""
+The backend type a kernel library dispatches on to reach this library: a
+`KernelInterface.Backend`, so Lava's backend-form queries (`Lava.matrix_shapes(b)`,
+`Lava.supports(b, s)`, `Lava.bestshape(b, ab, acc)`) reach `Lava.caps(b)`, which the Lava
+extension answers.
+"""
+struct B200Backend <: KI.Backend
     device::Int
 end
 B200Backend() = B200Backend(0)
@@ -396,12 +405,14 @@ end
     allgather!(recv, send, comm; stream = C_NULL)
 
 Enqueue on `stream`: `recv` (nranks × the bytes of `send`) receives every rank's `send` in
-rank order. Shards of equal size: pad a short last shard. With column-major Julia arrays a
+rank order. `recv` and `send` are any device values with `pointer`, `length` and `eltype`
+(a `B200Array`, a `Lava.LavaDeviceArray`). Shards of equal size: pad a short last shard. With column-major Julia arrays a
 gather of row shards is a gather of the shards of Cᵀ (compute Cᵀ = BᵀAᵀ per shard, or
 shard by output columns).
 """
-function allgather!(recv::B200Array{T}, send::B200Array{T}, comm::Comm;
-                    stream = C_NULL) where {T}
+function allgather!(recv, send, comm::Comm; stream = C_NULL)
+    T = eltype(send)
+    eltype(recv) === T || throw(ArgumentError("allgather!: recv and send element types differ"))
     nb = sizeof(T) * length(send)
     sizeof(T) * length(recv) == nb * comm.nranks ||
         throw(DimensionMismatch("recv must hold nranks × the elements of send"))

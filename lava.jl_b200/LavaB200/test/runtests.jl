@@ -26,6 +26,29 @@ using LinearAlgebra
         @test err isa LavaB200Error && err.operation == "lvb_gemm"
     end
 
+    @testset "B200Backend is a KernelInterface.Backend (no GPU)" begin
+        @test B200Backend() isa LavaB200.KI.Backend
+    end
+
+    # Lava's backend-form queries dispatch on `backend::KI.Backend` and reach `Lava.caps`
+    # (src/vocabulary/caps.jl:158-169, src/vocabulary/matrix.jl:138-141); with the extension
+    # loaded they answer for a B200 from the library's static sm_100a table.
+    if Base.find_package("Lava") !== nothing
+        @eval using Lava
+        @testset "Lava backend-form queries (no GPU)" begin
+            b = B200Backend()
+            shapes = Lava.matrix_shapes(b)
+            @test !isempty(shapes)
+            s = Lava.bestshape(b, Float16, Float32)
+            @test s isa Lava.MatrixShape && s.M == 16 && s.N == 16 && s.K == 16
+            @test Lava.supports(b, s)
+            @test Lava.bestshape(b, Int8, Int32) isa Lava.MatrixShape
+            @test Lava.bestshape(b, Float32, Float32) === nothing
+        end
+    else
+        @info "Lava not installed: backend-form query tests not run"
+    end
+
     @testset "shards and communicator ids (no GPU)" begin
         @test [shard_range(1000, 2, r; align = 128) for r in 0:1] == [(0, 512), (512, 488)]
         id = comm_unique_id()

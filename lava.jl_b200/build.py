@@ -13,6 +13,7 @@ import argparse
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -46,15 +47,22 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
     LIBDIR.mkdir(exist_ok=True)
     objdir = HERE / "_build"
     objdir.mkdir(exist_ok=True)
-    objs = []
     extra = ["-Xptxas", "-v"] if ptxas_v else []
-    for s in SOURCES:
+
+    def compile_one(s):
         obj = objdir / (Path(s).stem + ".o")
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-I", str(REPO / "include"), "-c", str(CSRC / s),
                "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        return s, obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    # The translation units are independent: compile them side by side (nvcc is
+    # single-threaded per file).
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 1)) as ex:
+        results = list(ex.map(compile_one, SOURCES))
+    objs = []
+    for s, obj, r in results:
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError(f"nvcc failed on {s}")

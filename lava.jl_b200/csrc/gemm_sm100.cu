@@ -1048,22 +1048,74 @@ constexpr size_t kNoAllocHeadBytes = 256;                   // DevStatus, padded
 constexpr size_t kNoAllocWorkspaceBytes = 16ull << 20;      // repack workspace: 16 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocHeadBytes + kNoAllocWorkspaceBytes];
 
-// Device address of g_noalloc_scratch, looked up once per device with that device current
-// (host code may not use the symbol itself as a device pointer).
-static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[128];
+// Identity of the calling thread's current CUDA context (cuCtxGetId through the runtime's
+// driver entry point; 0 when unavailable). A device reset destroys the primary context and
+// the next one has a new id, with the module — and the array — loaded afresh.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+static unsigned long long current_context_id() {
+  static std::once_flag once;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    cudaGetLastError();
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx &&
+      get_id(ctx, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
 
-static int noalloc_scratch(int device, void** out) {
-  const char* op = "lvb_gemm_noalloc";
+// Device address of g_noalloc_scratch, looked up once per device (and again if the device's
+// context was replaced, e.g. after cudaDeviceReset) with that device current: host code may
+// not use the symbol itself as a device pointer. The lookup loads this file's module when
+// CUDA loads modules lazily, which is when the array itself is placed on the device.
+struct NoallocScratch {
+  void* addr = nullptr;
+  unsigned long long ctx = 0;
+};
+static std::mutex g_noalloc_mu;
+static NoallocScratch g_noalloc[128];
+
+static int noalloc_scratch(int device, void** out, const char* op) {
   if (device < 0 || device >= 128) return fail(LVB_ERR_UNSUPPORTED, op, "device ordinal above 127");
+  // No context may be current on this thread yet (id 0): then the lookup runs, which makes
+  // the device's primary context current, and its id is recorded after it.
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[device]) {
+  NoallocScratch& slot = g_noalloc[device];
+  if (!slot.addr || ctx == 0 || slot.ctx != ctx) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return fail_cuda(e, op, "cudaGetSymbolAddress(scratch)");
-    g_noalloc_addr[device] = p;
+    slot.addr = p;
+    slot.ctx = current_context_id();
   }
-  *out = g_noalloc_addr[device];
+  *out = slot.addr;
+  return LVB_OK;
+}
+
+// The status word of lvb_gemm_noalloc on the current device (for its reader and self-test).
+int noalloc_status_word(DevStatus** out, const char* op) {
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess)
+    return fail(LVB_ERR_NO_DEVICE, op, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  void* scratch = nullptr;
+  int st = noalloc_scratch(device, &scratch, op);
+  if (st) return st;
+  *out = reinterpret_cast<DevStatus*>(scratch);
   return LVB_OK;
 }
 
@@ -1091,7 +1143,7 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   if (major != 10 || minor != 0)
     return fail(LVB_ERR_NO_DEVICE, op, "device is not sm_100", "run on a B200");
   void* scratch = nullptr;
-  st = noalloc_scratch(device, &scratch);
+  st = noalloc_scratch(device, &scratch, op);
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
@@ -1116,12 +1168,17 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   const size_t bytes_a = plan.repack_a ? (size_t)d->M * kp * es : 0;
   const size_t bytes_b = plan.repack_b ? (size_t)d->N * kp * es : 0;
   if (d->K > 0 && bytes_a + bytes_b > kNoAllocWorkspaceBytes) {
-    char buf[200];
+    // 8-bit operands stored MN-contiguous (A column-major, B row-major) are copied K-major
+    // at any alignment, so alignment alone cannot avoid the workspace for them.
+    const bool mn8 = es == 1 && ((plan.repack_a && !d->a_rowmajor) || (plan.repack_b && d->b_rowmajor));
+    char buf[240];
     std::snprintf(buf, sizeof buf,
-                  "operands to repack need %zu bytes, above the %zu-byte static workspace",
-                  bytes_a + bytes_b, (size_t)kNoAllocWorkspaceBytes);
+                  "operands to repack need %zu bytes, above the %zu-byte static workspace%s",
+                  bytes_a + bytes_b, (size_t)kNoAllocWorkspaceBytes,
+                  mn8 ? " (an 8-bit operand stored MN-contiguous is always copied K-major)" : "");
     return fail(LVB_ERR_UNSUPPORTED, op, buf,
-                "pass 16-byte aligned operands with 16-byte multiple leading dimensions, or use lvb_gemm");
+                mn8 ? "store 8-bit A row-major and B column-major (K-contiguous), or use lvb_gemm"
+                    : "pass 16-byte aligned operands with 16-byte multiple leading dimensions, or use lvb_gemm");
   }
 
   // The status word must start at zero for this call; the array keeps the last call's bytes.
@@ -1156,6 +1213,28 @@ extern "C" int lvb_gemm_noalloc(const lvb_gemm_desc* d, const void* A, const voi
   }
   plan.repack_a = plan.repack_b = 0;
   return gemm_launch_aligned(&d2, plan, a, b, C, nullptr, s, &local);
+}
+
+extern "C" int lvb_gemm_noalloc_status(void* stream, int32_t* code, int32_t* where,
+                                       int32_t* block) {
+  using namespace lvb;
+  const char* op = "lvb_gemm_noalloc_status";
+  DevStatus* word = nullptr;
+  int st = noalloc_status_word(&word, op);
+  if (st) return st;
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e, op, "cudaStreamSynchronize");
+  DevStatus h;
+  e = cudaMemcpy(&h, word, sizeof h, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail_cuda(e, op, "reading the status word");
+  if (h.code != 0) {
+    e = cudaMemset(word, 0, sizeof(DevStatus));
+    if (e != cudaSuccess) return fail_cuda(e, op, "clearing the status word");
+  }
+  if (code) *code = h.code;
+  if (where) *where = h.where;
+  if (block) *block = h.block;
+  return LVB_OK;
 }
 
 namespace lvb {

@@ -80,6 +80,12 @@ int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A
 int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
                        cudaStream_t stream);
 
+// The status word at the head of lvb_gemm_noalloc's static scratch array, on the current
+// device (looked up without allocating).
+int noalloc_status_word(DevStatus** out, const char* op);
+// Enqueue the bounded-wait self-test kernel against `status` (see selftest.cu).
+int selftest_launch(DevStatus* status, int32_t timeout_ms, cudaStream_t stream, const char* op);
+
 // ---- matrix-vector products (gemv_sm100.cu): lvb_gemm with N == 1 or M == 1 ----
 struct GemvPlan {
   int32_t k_contiguous;     // the matrix runs along k (one warp per row) or along rows

@@ -24,6 +24,14 @@ __global__ void wait_selftest_kernel(DevStatus* status, unsigned long long timeo
   __syncthreads();
 }
 
+int selftest_launch(DevStatus* status, int32_t timeout_ms, cudaStream_t stream, const char* op) {
+  if (timeout_ms <= 0 || timeout_ms > 2000)
+    return fail(LVB_ERR_INVALID_ARG, op, "timeout_ms must be in 1..2000");
+  wait_selftest_kernel<<<1, 32, 0, stream>>>(status, (unsigned long long)timeout_ms * 1000000ull);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LVB_OK : fail_cuda(e, op, "kernel launch");
+}
+
 }  // namespace lvb
 
 using namespace lvb;
@@ -34,8 +42,17 @@ extern "C" int lvb_selftest_wait_timeout(int32_t timeout_ms, void* stream) {
     return fail(LVB_ERR_INVALID_ARG, op, "timeout_ms must be in 1..2000");
   DeviceState* dev = current_device_state(op);
   if (!dev) return LVB_ERR_NO_DEVICE;
-  wait_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      dev->status, (unsigned long long)timeout_ms * 1000000ull);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? LVB_OK : fail_cuda(e, op, "kernel launch");
+  return selftest_launch(dev->status, timeout_ms, reinterpret_cast<cudaStream_t>(stream), op);
+}
+
+// The same against lvb_gemm_noalloc's own status word (the head of its static array), which
+// lvb_gemm_noalloc_status reads. Allocates nothing.
+extern "C" int lvb_gemm_noalloc_selftest_wait_timeout(int32_t timeout_ms, void* stream) {
+  const char* op = "lvb_gemm_noalloc_selftest_wait_timeout";
+  if (timeout_ms <= 0 || timeout_ms > 2000)
+    return fail(LVB_ERR_INVALID_ARG, op, "timeout_ms must be in 1..2000");
+  DevStatus* word = nullptr;
+  int st = noalloc_status_word(&word, op);
+  if (st) return st;
+  return selftest_launch(word, timeout_ms, reinterpret_cast<cudaStream_t>(stream), op);
 }

@@ -46,6 +46,7 @@ DTYPE_SIZES = {F16: 2, BF16: 2, F32: 4, I8: 1, U8: 1, I32: 4, U32: 4}
 EXPORTS = [
     "lvb_caps_sm100", "lvb_caps", "lvb_matrix_shapes", "lvb_bestshape",
     "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm", "lvb_gemm_noalloc",
+    "lvb_gemm_noalloc_status", "lvb_gemm_noalloc_selftest_wait_timeout",
     "lvb_gemm_ex_check", "lvb_gemm_ex",
     "lvb_attention_check", "lvb_attention_plan_for", "lvb_attention_fwd",
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
@@ -144,6 +145,9 @@ def _load() -> C.CDLL:
         "lvb_gemm_plan_for": ([C.POINTER(lvb_gemm_desc), C.c_int32, C.POINTER(lvb_gemm_plan)], C.c_int),
         "lvb_gemm": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
         "lvb_gemm_noalloc": ([C.POINTER(lvb_gemm_desc), P, P, P, P], C.c_int),
+        "lvb_gemm_noalloc_status": ([P, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_int32)], C.c_int),
+        "lvb_gemm_noalloc_selftest_wait_timeout": ([C.c_int32, P], C.c_int),
         "lvb_gemm_ex_check": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue)], C.c_int),
         "lvb_gemm_ex": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue), P, P, P, P], C.c_int),
         "lvb_attention_check": ([C.POINTER(lvb_attn_desc)], C.c_int),
@@ -473,6 +477,14 @@ def device_status(stream=None):
     """Synchronise and read/clear the device status word: (code, where, block)."""
     code, where, block = C.c_int32(), C.c_int32(), C.c_int32()
     check(lib.lvb_device_status(_stream_ptr(stream), C.byref(code), C.byref(where), C.byref(block)))
+    return code.value, where.value, block.value
+
+
+def gemm_noalloc_status(stream=None):
+    """Synchronise and read/clear lvb_gemm_noalloc's own status word: (code, where, block)."""
+    code, where, block = C.c_int32(), C.c_int32(), C.c_int32()
+    check(lib.lvb_gemm_noalloc_status(_stream_ptr(stream), C.byref(code), C.byref(where),
+                                      C.byref(block)))
     return code.value, where.value, block.value
 
 

@@ -33,16 +33,38 @@ def attention_units(B: int, Hkv: int, world: int, rank: int) -> list[tuple[int, 
     return [divmod(u, Hkv) for u in range(b0, b0 + n)]
 
 
-def allgather_rows(local, group=None):
-    """Concatenate every rank's contiguous row block (row-major C shards of equal size)
-    on every rank with one all_gather_into_tensor (NCCL on GPUs, gloo on CPU)."""
+def allgather_rows(local, total: int | None = None, align: int = GEMM_ROW_ALIGN, group=None):
+    """Concatenate every rank's contiguous row block of a row-major output on every rank with
+    one all_gather_into_tensor (NCCL on GPUs, gloo on CPU).
+
+    ``total``: the rows of the whole output when the shards come from
+    ``shard_range(total, world, rank, align)`` (``gemm_rows``): their sizes may differ (the
+    ragged last chunk, or one chunk more on the lower ranks), so each rank pads its block to
+    the largest share, and the padding is dropped from the gathered result. Without ``total``
+    every rank's block must have the same number of rows."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
-    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
-                      device=local.device)
-    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
-    return out
+    rest = tuple(local.shape[1:])
+    if total is None:
+        counts = [local.shape[0]] * world
+    else:
+        counts = [shard_range(total, world, r, align)[1] for r in range(world)]
+        rank = dist.get_rank(group)
+        if counts[rank] != local.shape[0]:
+            raise ValueError(f"rank {rank} holds {local.shape[0]} rows, its share of {total} "
+                             f"is {counts[rank]}")
+    width = max(counts) if counts else 0
+    send = local.contiguous()
+    if send.shape[0] != width:
+        padded = torch.zeros((width,) + rest, dtype=local.dtype, device=local.device)
+        padded[:send.shape[0]] = send
+        send = padded
+    out = torch.empty((world * width,) + rest, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, send, group=group)
+    if all(c == width for c in counts):
+        return out
+    return torch.cat([out[r * width:r * width + counts[r]] for r in range(world)])
 
 
 class Comm:

@@ -50,6 +50,32 @@ def attention_ref(Q, K, V, causal: bool, scale: float, return_lse: bool = False)
     return (O, L) if return_lse else O
 
 
+def attention_rows(q, k, v, rows, causal: bool, scale: float, sq: int | None = None):
+    """The float64 definition for the query rows ``rows`` of one (b, h) unit only:
+    q [Sq,D] (or just the selected rows with ``sq`` the unit's full Sq), k/v [Skv,D].
+    Returns (O [len(rows),D], lse [len(rows)]). Each row reads only the keys it may see, so
+    checking a few hundred rows of a 16k-key head costs a few hundred key rows' products."""
+    rows = np.asarray(rows)
+    Skv = k.shape[0]
+    Sq = q.shape[0] if sq is None else sq
+    qs = (q if sq is not None else q[rows]).astype(np.float64)
+    last = int(rows.max()) + (Skv - Sq) if causal else Skv - 1
+    kk = k[:max(0, min(Skv, last + 1))].astype(np.float64)
+    vv = v[:kk.shape[0]].astype(np.float64)
+    s = scale * (qs @ kk.T)
+    if causal:
+        j = np.arange(kk.shape[0])[None, :]
+        s = np.where(j <= rows[:, None] + (Skv - Sq), s, -np.inf)
+    mx = s.max(axis=1, keepdims=True) if s.shape[1] else np.full((len(rows), 1), -np.inf)
+    ok = np.isfinite(mx[:, 0])
+    mx = np.where(np.isfinite(mx), mx, 0.0)
+    p = np.exp(s - mx)
+    l = p.sum(axis=1)
+    O = np.where(ok[:, None], (p @ vv) / np.where(l > 0, l, 1.0)[:, None], 0.0)
+    lse = np.where(ok, mx[:, 0] + np.log(np.where(l > 0, l, 1.0)), -np.inf)
+    return O, lse
+
+
 def attention_blockwise(q, k, v, causal: bool, scale: float, block: int = 128):
     """One (b, h) unit in float32, online softmax over key blocks. q [Sq,D], k/v [Skv,D].
     Returns (O [Sq,D] float32, lse [Sq] float32)."""

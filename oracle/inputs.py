@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .vocab import round_bf16
+from .vocab import round_bf16, f32_to_bf16_bits
 
 GEMM_CONFIGS = {
     "C1": dict(M=512, N=512, K=512, ab="Float16", out="Float32", seed=0),
@@ -68,4 +68,56 @@ def attention_inputs(B: int, Hq: int, Hkv: int, S: int, D: int, dtype: str, seed
     Q = cast(g.standard_normal(size=(B, Hq, S, D), dtype=np.float32), dtype)
     K = cast(g.standard_normal(size=(B, Hkv, Skv, D), dtype=np.float32), dtype)
     V = cast(g.standard_normal(size=(B, Hkv, Skv, D), dtype=np.float32), dtype)
+    return Q, K, V
+
+
+def _operand_stored(g: np.random.Generator, rows: int, K: int, ab: str, chunk: int):
+    """One operand's storage array, drawn ``chunk`` rows at a time from ``g``. A uniform
+    draw takes one 64-bit output per element in order, so the chunks continue the same stream
+    and the bytes equal one draw of the whole array. 16-bit floats come back as their stored
+    bits: float16, or uint16 bf16 bits (half the memory of float32 values)."""
+    if ab in ("Int8", "UInt8"):
+        lo, hi, dt = (-128, 128, np.int8) if ab == "Int8" else (0, 256, np.uint8)
+        out = np.empty((rows, K), dtype=dt)
+        if (chunk * K) % 2:
+            chunk = rows   # 16-bit integer draws share 32-bit outputs: keep chunks even
+        for r in range(0, rows, chunk):
+            n = min(chunk, rows - r)
+            out[r:r + n] = g.integers(lo, hi, size=(n, K), dtype=np.int16).astype(dt)
+        return out
+    out = np.empty((rows, K), dtype=np.float16 if ab == "Float16" else np.uint16)
+    for r in range(0, rows, chunk):
+        n = min(chunk, rows - r)
+        x = g.uniform(-1.0, 1.0, size=(n, K)).astype(np.float32)
+        out[r:r + n] = x.astype(np.float16) if ab == "Float16" else f32_to_bf16_bits(x)
+    return out
+
+
+def gemm_inputs_stored(M: int, N: int, K: int, ab: str, seed: int, chunk: int = 2048):
+    """``gemm_inputs`` for the large configurations: the same bytes, generated in row chunks
+    so the float64 draw never holds more than ``chunk`` rows; BFloat16 operands are returned
+    as uint16 bit arrays (see ``vocab.bf16_bits_to_f32``)."""
+    g = rng(seed)
+    A = _operand_stored(g, M, K, ab, chunk)
+    Bt = _operand_stored(g, N, K, ab, chunk)
+    return A, Bt
+
+
+def attention_inputs_stored(B: int, Hq: int, Hkv: int, S: int, D: int, dtype: str, seed: int,
+                            Skv: int | None = None):
+    """``attention_inputs`` for the large configurations: the same values, drawn one batch
+    index at a time (sequential normal draws continue the same stream), returned as the
+    stored 16-bit patterns (float16, or uint16 bf16 bits)."""
+    g = rng(seed)
+    Skv = S if Skv is None else Skv
+
+    def draw(H, L):
+        out = np.empty((B, H, L, D), dtype=np.float16 if dtype == "Float16" else np.uint16)
+        for b in range(B):
+            x = g.standard_normal(size=(H, L, D), dtype=np.float32)
+            out[b] = x.astype(np.float16) if dtype == "Float16" else f32_to_bf16_bits(x)
+        return out
+    Q = draw(Hq, S)
+    K = draw(Hkv, Skv)
+    V = draw(Hkv, Skv)
     return Q, K, V

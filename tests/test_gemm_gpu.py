@@ -219,16 +219,87 @@ def test_deterministic_and_canary(lvb, torch_cuda):
     assert torch.all(big[:, 333:] == -5.0)
 
 
+def row_checksum_bound(C, out):
+    """Bound on |sum_n C[m,n] - sum_n exact[m,n]| per row m, for a C rounded once to `out`
+    from an fp32 accumulator. Each element's rounding error is uniform within half an output
+    ulp (variance ulp^2/12) and independent of the others, so the row's error has standard
+    deviation sqrt(sum_n ulp^2/12); 8 of those, plus 2^-16 of sum_n |C| for the fp32
+    accumulation (whose error per element is ~2^-24·sqrt(K)·|C|, under 2^-16·|C| for K <= 2^16).
+    A single element off by one part in a thousand of a typical |C| already exceeds it."""
+    C64 = np.asarray(C, dtype=np.float64)
+    ulp = out_ulp(C64, out) if out != "Float32" else np.zeros_like(C64)
+    return 8.0 * np.sqrt((ulp ** 2).sum(axis=1) / 12.0) + 2.0 ** -16 * np.abs(C64).sum(axis=1) + 1e-9
+
+
+def check_row_checksums(C, A_rows_f64, colsum_f64, out):
+    """Every row at once: sum_n C[m,n] against A[m,:]·(sum_n B[:,n]) in float64 (exact for
+    fp16/bf16 inputs up to float64 rounding of the row sums)."""
+    got = np.asarray(C, dtype=np.float64).sum(axis=1)
+    want = A_rows_f64 @ colsum_f64
+    bound = row_checksum_bound(C, out)
+    bad = np.abs(got - want) > bound
+    assert not bad.any(), (f"{int(bad.sum())} row checksums off; worst "
+                           f"{float(np.max(np.abs(got - want) - bound)):.3e} over the bound")
+
+
+def band_rows(M, bands, seed, band=256):
+    """First and last row of `bands` randomly chosen `band`-row tile bands, plus rows 0 and
+    M-1: the rows at the edges of the kernel's output tiles."""
+    starts = np.random.default_rng(seed).choice(M // band, bands, replace=False) * band
+    return np.unique(np.concatenate([starts, starts + band - 1, [0, M - 1]]))
+
+
 @pytest.mark.slow
-def test_config2_fp16_8192_sampled_rows(lvb, torch_cuda):
-    """C2 at full size: every output row sampled is checked against the float64 oracle."""
+def test_config2_fp16_8192_sampled_rows_and_row_checksums(lvb, torch_cuda):
+    """C2 at full size: 130 sampled rows (both edges of 64 tile bands) checked element by
+    element against the float64 oracle, and every row through its checksum."""
     torch = torch_cuda
     cfg = GEMM_CONFIGS["C2"]
     A, Bt = gemm_inputs(cfg["M"], cfg["N"], cfg["K"], cfg["ab"], cfg["seed"])
-    C = run(lvb, torch, A, Bt, "Float16", "Float16")
-    rows = np.random.default_rng(0).choice(cfg["M"], 96, replace=False)
-    rows = np.concatenate([rows, [0, 127, 128, cfg["M"] - 1]])
+    C = run(lvb, torch, A, Bt, "Float16", "Float16", c_rowmajor=True)
+    rows = band_rows(cfg["M"], 64, seed=0)
+    assert len(rows) >= 128
     check(C[rows], A[rows], Bt.T, "Float16")
+    colsum = Bt.astype(np.float64).sum(axis=0)
+    check_row_checksums(C, A.astype(np.float64), colsum, "Float16")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("out,c_rowmajor", [("BFloat16", True), ("Float32", False)])
+def test_config5_bf16_gemm_65536_full(lvb, torch_cuda, out, c_rowmajor):
+    """C5's GEMM at its stated size: A 65536x8192 row-major, B 8192x8192 column-major,
+    U[-1,1) from PCG64 seed 5 rounded to bf16, on the CTA-pair kernel (row-major C: the
+    65536 rows are the kernel's tile rows; column-major C: its tile columns). 130 rows at
+    the edges of 64 tile bands are checked element by element against the float64 oracle
+    (rounded once to bf16, or exact for the fp32 variant with the north star's |Δ| <= 1e-2),
+    every row through its checksum."""
+    torch = torch_cuda
+    cfg = GEMM_CONFIGS["C5g"]
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    from oracle.inputs import gemm_inputs_stored
+    Abits, Btbits = gemm_inputs_stored(M, N, K, "BFloat16", cfg["seed"])
+    plan = lvb.gemm_plan(M, N, K, lvb.BF16, lvb.BF16 if out == "BFloat16" else lvb.F32,
+                         c_rowmajor=c_rowmajor)
+    assert plan.cta_pair == 1
+    dA = torch.from_numpy(Abits.view(np.int16)).cuda().view(torch.bfloat16)
+    dB = torch.from_numpy(Btbits.view(np.int16)).cuda().view(torch.bfloat16)
+    odt = torch.bfloat16 if out == "BFloat16" else torch.float32
+    dC = (torch.empty((M, N), dtype=odt, device="cuda") if c_rowmajor
+          else torch.empty((N, M), dtype=odt, device="cuda").t())
+    lvb.gemm(dC, dA, dB.t())
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    del dA, dB
+    C = dC.float().cpu().numpy()
+    del dC
+    rows = band_rows(M, 64, seed=5)
+    assert len(rows) >= 128
+    Bv = vocab.bf16_bits_to_f32(Btbits)           # (N, K) values
+    check(C[rows], vocab.bf16_bits_to_f32(Abits[rows]), Bv.T, out)
+    colsum = Bv.astype(np.float64).sum(axis=0)
+    for r0 in range(0, M, 8192):
+        A64 = vocab.bf16_bits_to_f32(Abits[r0:r0 + 8192]).astype(np.float64)
+        check_row_checksums(C[r0:r0 + 8192], A64, colsum, out)
 
 
 @pytest.mark.slow

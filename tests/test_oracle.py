@@ -231,3 +231,37 @@ def test_epilogue_ref_is_perelement_over_the_accumulator():
     want = vocab.coopmat_convert(vocab.coopmat_perelement(f, acc), "Float16")
     got = gemm_epilogue_ref(A, B, "Float16", bias, "col", res, "gelu")
     assert np.array_equal(got, want)
+
+
+def test_chunked_generators_match_the_one_shot_draw():
+    """The full-size parity tests draw their inputs in chunks (``gemm_inputs_stored``,
+    ``attention_inputs_stored``); the bytes must equal one draw of the whole arrays."""
+    from oracle.inputs import (gemm_inputs, gemm_inputs_stored, attention_inputs,
+                               attention_inputs_stored)
+    from oracle.vocab import bf16_bits_to_f32
+    for ab in ("Float16", "BFloat16", "Int8", "UInt8"):
+        A, Bt = gemm_inputs(301, 77, 96, ab, seed=11)
+        A2, B2 = gemm_inputs_stored(301, 77, 96, ab, seed=11, chunk=13)
+        if ab == "BFloat16":
+            A2, B2 = bf16_bits_to_f32(A2), bf16_bits_to_f32(B2)
+        assert np.array_equal(A, A2) and np.array_equal(Bt, B2), ab
+    for T in ("Float16", "BFloat16"):
+        ref = attention_inputs(3, 4, 2, 40, 32, T, seed=4, Skv=56)
+        got = attention_inputs_stored(3, 4, 2, 40, 32, T, seed=4, Skv=56)
+        if T == "BFloat16":
+            got = [bf16_bits_to_f32(x) for x in got]
+        assert all(np.array_equal(a, b) for a, b in zip(ref, got)), T
+
+
+def test_attention_rows_matches_the_full_definition():
+    from oracle.attention import attention_ref, attention_rows
+    from oracle.inputs import attention_inputs
+    for Sq, Skv in ((300, 300), (200, 333), (400, 100)):
+        Q, K, V = attention_inputs(1, 1, 1, Sq, 64, "Float16", seed=Sq, Skv=Skv)
+        O, L = attention_ref(Q, K, V, True, 0.125, return_lse=True)
+        rows = np.array([0, 1, Sq // 2, Sq - 1])
+        o, l = attention_rows(Q[0, 0], K[0, 0], V[0, 0], rows, True, 0.125)
+        assert np.allclose(o, O[0, 0][rows], atol=1e-12, rtol=0)
+        fin = np.isfinite(L[0, 0][rows])
+        assert np.array_equal(np.isfinite(l), fin)
+        assert np.allclose(l[fin], L[0, 0][rows][fin], atol=1e-12, rtol=0)

@@ -62,6 +62,15 @@ def _worker(rank, world, port, q):
         local = torch.from_numpy(gemm_ref(A[r0:r0 + rn], Bt.T, "Int32"))
         full = allgather_rows(local)
         ok_gemm = np.array_equal(full.numpy(), gemm_ref(A, Bt.T, "Int32"))
+        # uneven shares (1000 rows: 512 + 488): padded to the largest share for the gather,
+        # the padding dropped from the result
+        M2 = 1000
+        A2, Bt2 = gemm_inputs(M2, N, K, "Int8", seed=8)
+        r0, rn = gemm_rows(M2, world, rank)
+        local2 = torch.from_numpy(gemm_ref(A2[r0:r0 + rn], Bt2.T, "Int32"))
+        full2 = allgather_rows(local2, total=M2)
+        ok_gemm &= tuple(full2.shape) == (M2, N)
+        ok_gemm &= np.array_equal(full2.numpy(), gemm_ref(A2, Bt2.T, "Int32"))
         # attention: (batch, kv-head) units, each with its group of query heads
         Q, Kt, V = attention_inputs(2, 4, 2, 64, 64, "Float16", seed=4)
         ref = attention_ref(Q, Kt, V, True, 0.125)
