@@ -359,11 +359,20 @@ def make_gemm(torch, lvb, w, rank):
         else:
             lvb.gemm(d_outs[0], view_a(d_ins[0]), view_b(d_ins[1]), stream=stream)
 
-    def step():
-        call(ins, outs)
+    # the timed step: the same call, described once (lvb.prepare_gemm: one foreign call per
+    # launch); e2e goes through lvb.gemm every step
+    if act:
+        prepared = lvb.prepare_gemm(Cs, view_a(As), view_b(Bs), bias=ins[2], residual=ins[3],
+                                    activation=act)
+    else:
+        prepared = lvb.prepare_gemm(Cs, view_a(As), view_b(Bs))
+
+    def step(stream=None):
+        prepared(stream)
 
     def compute(d_ins, d_outs, stream):
         call(d_ins, d_outs, stream)
+    step.plain = lambda: call(ins, outs)
     return step, compute, ins, outs
 
 
@@ -593,6 +602,37 @@ def measure_extras(args, torch, lvb, world, rank, local, stream, sync, max_over_
     return out
 
 
+def host_path_breakdown(torch, step, stream, n=2000, graph_calls=100):
+    def per_call_us(fn, calls):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(calls):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / calls
+    out = {"lvb_gemm_us": per_call_us(step.plain, n), "prepared_us": per_call_us(step, n)}
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=side):
+            for _ in range(graph_calls):
+                step(side)
+    torch.cuda.synchronize()
+    out["graph_replay_us"] = per_call_us(g.replay, 20) / graph_calls
+    out["how"] = ("device time per call over back-to-back calls: lvb.gemm (descriptor built "
+                  "in Python each call), lvb.prepare_gemm (one foreign call), and a CUDA graph "
+                  f"of {graph_calls} captured prepared calls (~ the kernel's own time)")
+    del g
+    return out
+
+
 def cublas_sanity(torch, w, ins, steps, warmup, stream):
     """torch.matmul (cuBLAS) on the headline GEMM's operands in the same kind of timed
     region: a library figure beside the kernel's, not part of `value`."""
@@ -751,6 +791,13 @@ def run_gpu(args, w):
                    "how": "lvb_gemm without epilogue, then torch elementwise "
                           f"{w['epilogue']}(C + bias + R) as a second pass over C"}
 
+    # host path of a small GEMM: per-call device time through lvb.gemm (Python wrapper each
+    # call), through the prepared call (the timed step), and replayed from a CUDA graph of
+    # captured calls (about the kernel's own time)
+    per_call = None
+    if w["kind"] == "gemm" and w["M"] * w["N"] * w["K"] <= 1 << 30 and not args.no_extras:
+        per_call = host_path_breakdown(torch, step, stream)
+
     cublas = None
     if not args.no_extras:
         cublas = cublas_sanity(torch, w, ins, args.steps, args.warmup, stream)
@@ -828,6 +875,8 @@ def run_gpu(args, w):
             line["unfused_comparison"] = unfused
         if cublas:
             line["cublas"] = cublas
+        if per_call:
+            line["per_call"] = per_call
         if extras:
             line.update(extras)
         print(json.dumps(line), flush=True)

@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define LVB_ABI_VERSION 4
+#define LVB_ABI_VERSION 5
 
 typedef enum lvb_status {
   LVB_OK = 0,
@@ -164,14 +164,17 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
  * across CTAs with partial sums in a stream-ordered workspace. */
 int lvb_gemm(const lvb_gemm_desc* d, const void* A, const void* B, void* C, void* stream);
 
-/* Fused epilogue: C = act(A·B + bias + R), computed in fp32 and converted once to C's type.
+/* Fused epilogue: C = f(act((A·B + bias + R) ⊙ S)), computed in fp32 and converted once to
+ * C's type, with A·B taken over the padded k extent when k_pad > K (the clamp modes).
  * The accumulator starting from bias + residual is Lava's coopmat_add accumulator
  * initialisation — the bias loaded at stride 0 so every column (or row) reads the same
  * vector, the residual at its own leading dimension (src/device/coopmat_intrinsics.jl:
  * 435-447; src/compiler/spirv/coopmat.jl:873-878) — and `act` the per-element function a
  * GEMM applies to its accumulator with coopmat_perelement / getcomp+setcomp (coopmat_
  * intrinsics.jl:322-331,551-593) before convert and copyto! (src/vocabulary/coopmat.jl:
- * 166-176). Floating-point outputs only (coopmat_add is OpFAdd). */
+ * 166-176); S the coopmat_mul operand and f the caller's per-element program. Bias, residual,
+ * S, activation and program need a floating-point output (coopmat_add and coopmat_mul are
+ * OpFAdd / OpFMul); the clamp modes apply to every pair, integer ones exactly. */
 typedef enum lvb_activation {
   LVB_ACT_NONE = 0,
   LVB_ACT_RELU = 1,       /* x < 0 ? 0 : x */
@@ -185,6 +188,73 @@ typedef enum lvb_bias_axis {
   LVB_BIAS_PER_COL = 1    /* bias[j] added to column j: N elements (row-major stride-0 load) */
 } lvb_bias_axis;
 
+/* Tensor clamp modes of the operands' loads (src/vocabulary/tensor.jl:46-51). */
+typedef enum lvb_clamp {
+  LVB_CLAMP_UNDEFINED = 0, /* a read past the extent is undefined; this library reads 0 */
+  LVB_CLAMP_CONSTANT = 1,  /* reads the clamp value, rounded to the operand's type
+                              (tensor_clampbits, tensor.jl:83-85) */
+  LVB_CLAMP_TO_EDGE = 2    /* reads the nearest element inside the operand */
+} lvb_clamp;
+
+/* A caller-supplied per-element function, Lava's coopmat_perelement(f, m, extras...)
+ * (src/device/coopmat_intrinsics.jl:520-678): f(row0, col0, elem, extra) evaluated for every
+ * element of the result, with 0-based row and column of C (coopmat_intrinsics.jl:551-593),
+ * the element, and the element at the same position of an optional second matrix (the
+ * matrix-operand form). Written as a straight-line program over 8 registers of 32 bits; at
+ * its start r0 = the element (float), r1 = row (int32), r2 = col (int32), r3 = the extra
+ * matrix's element (float, 0 without one), r4..r7 = 0; its result is r0 (float). Float
+ * operations round as IEEE fp32 (exp/log/tanh/erf within a few ulp of the correctly rounded
+ * value); integer operations wrap as int32. */
+#define LVB_PE_MAX_INSTR 32
+#define LVB_PE_REGS 8
+typedef enum lvb_pe_op {
+  LVB_PE_CONST = 0,   /* r[dst] = the fp32 value with bits imm */
+  LVB_PE_ICONST = 1,  /* r[dst] = (int32)imm */
+  LVB_PE_MOV = 2,     /* r[dst] = r[a] */
+  LVB_PE_FADD = 3,    /* r[dst] = r[a] + r[b] (fp32) */
+  LVB_PE_FSUB = 4,
+  LVB_PE_FMUL = 5,
+  LVB_PE_FDIV = 6,
+  LVB_PE_FMIN = 7,    /* fminf / fmaxf: a NaN operand yields the other */
+  LVB_PE_FMAX = 8,
+  LVB_PE_FFMA = 9,    /* r[dst] = fma(r[a], r[b], r[dst]) */
+  LVB_PE_FNEG = 10,   /* r[dst] = f(r[a]) for the unary functions below */
+  LVB_PE_FABS = 11,
+  LVB_PE_FEXP = 12,
+  LVB_PE_FEXP2 = 13,
+  LVB_PE_FLOG = 14,
+  LVB_PE_FTANH = 15,
+  LVB_PE_FSQRT = 16,
+  LVB_PE_FRSQRT = 17,
+  LVB_PE_FFLOOR = 18,
+  LVB_PE_FERF = 19,
+  LVB_PE_I2F = 20,    /* r[dst] = (float)(int32)r[a] (RNE) */
+  LVB_PE_IADD = 21,   /* r[dst] = r[a] + r[b] (int32, wrapping) */
+  LVB_PE_ISUB = 22,
+  LVB_PE_IMUL = 23,
+  LVB_PE_IMIN = 24,
+  LVB_PE_IMAX = 25,
+  LVB_PE_FLT = 26,    /* r[dst] = (r[a] < r[b]) ? 1 : 0 (int32 result; fp32 comparison) */
+  LVB_PE_FLE = 27,
+  LVB_PE_FEQ = 28,
+  LVB_PE_ILT = 29,    /* the same with int32 operands */
+  LVB_PE_ILE = 30,
+  LVB_PE_IEQ = 31,
+  LVB_PE_SELECT = 32, /* r[dst] = r[a] != 0 ? r[b] : r[dst] (bitwise test of the word) */
+  LVB_PE_NUM_OPS = 33
+} lvb_pe_op;
+
+typedef struct lvb_pe_instr {
+  uint8_t op;         /* lvb_pe_op */
+  uint8_t dst, a, b;  /* registers 0..7 (unused operands 0) */
+  uint32_t imm;       /* LVB_PE_CONST: fp32 bits; LVB_PE_ICONST: int32 */
+} lvb_pe_instr;
+
+typedef struct lvb_pe_program {
+  int32_t n;          /* instructions used, 0..LVB_PE_MAX_INSTR */
+  lvb_pe_instr code[LVB_PE_MAX_INSTR];
+} lvb_pe_program;
+
 typedef struct lvb_epilogue {
   const void* bias;       /* NULL: none. Contiguous vector of bias_type */
   const void* residual;   /* NULL: none. M×N in C's layout, leading dimension ldr; may be C
@@ -194,8 +264,31 @@ typedef struct lvb_epilogue {
   int32_t bias_axis;      /* lvb_bias_axis */
   int32_t residual_type;  /* LVB_F32 | LVB_F16 | LVB_BF16 */
   int32_t activation;     /* lvb_activation */
+  /* coopmat_mul (src/device/coopmat_intrinsics.jl:402-464): the accumulator multiplied
+   * element-wise by S, M×N in C's layout with leading dimension ldm (NULL: none). */
+  const void* mul;
+  int64_t ldm;
+  int32_t mul_type;       /* LVB_F32 | LVB_F16 | LVB_BF16 */
+  int32_t extra_type;     /* LVB_F32 | LVB_F16 | LVB_BF16 */
+  /* the matrix operand of the per-element program (r3), M×N in C's layout (NULL: none) */
+  const void* extra;
+  int64_t lde;
+  const lvb_pe_program* program;  /* NULL: none. Read during the call only. */
+  /* Clamped operand loads over a padded k extent: the product runs over k_pad >= K columns
+   * of A and rows of B, and the reads past K take each operand's clamp mode — what a Lava
+   * kernel computes when its k loop steps a tile that does not divide K through tensor
+   * layouts with these clamps (tensor_intrinsics.jl:139-148). k_pad 0 (or K): no padding,
+   * clamps unused. Rows past M and columns past N are never stored, so only the k tail of
+   * each operand is read through its clamp. */
+  int64_t k_pad;
+  int32_t a_clamp;        /* lvb_clamp of A's reads past column K-1 */
+  int32_t b_clamp;        /* lvb_clamp of B's reads past row K-1 */
+  double a_clamp_value;   /* LVB_CLAMP_CONSTANT: the value (integer types: an integer in range) */
+  double b_clamp_value;
 } lvb_epilogue;
 
+/* Validate a per-element program: instruction count, opcodes, registers (host only). */
+int lvb_pe_program_check(const lvb_pe_program* program);
 /* Validate a descriptor with its epilogue (host only; `e` may be NULL). */
 int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e);
 /* lvb_gemm with the fused epilogue `e` (NULL: exactly lvb_gemm). With K == 0 the result is

@@ -418,16 +418,53 @@ int lvb_gemm_check(const lvb_gemm_desc* d) {
 
 static bool float_type(int t) { return t == LVB_F32 || t == LVB_F16 || t == LVB_BF16; }
 
+// An M×N epilogue matrix in C's layout (residual, S, the program's extra operand).
+static int check_cmatrix(const char* op, const lvb_gemm_desc* d, const void* ptr, int type,
+                         int64_t ld, const char* what, const char* ld_name) {
+  if (!float_type(type)) {
+    return fail(LVB_ERR_UNSUPPORTED, op,
+                std::string(what) + " type must be Float32, Float16 or BFloat16");
+  }
+  const int64_t rmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
+  if (ld < rmin)
+    return fail(LVB_ERR_INVALID_ARG, op, std::string(ld_name) + (d->c_rowmajor ? " < N" : " < M"));
+  if ((uintptr_t)ptr % dtype_size(type))
+    return fail(LVB_ERR_INVALID_ARG, op, std::string(what) + " not aligned to its element size");
+  return LVB_OK;
+}
+
+int lvb_pe_program_check(const lvb_pe_program* prog) {
+  const char* op = "lvb_pe_program";
+  if (!prog) return fail(LVB_ERR_INVALID_ARG, op, "program is NULL");
+  if (prog->n < 0 || prog->n > LVB_PE_MAX_INSTR)
+    return fail(LVB_ERR_INVALID_ARG, op, "instruction count outside 0..32");
+  for (int i = 0; i < prog->n; ++i) {
+    const lvb_pe_instr& I = prog->code[i];
+    char buf[96];
+    if (I.op >= LVB_PE_NUM_OPS) {
+      std::snprintf(buf, sizeof buf, "instruction %d: unknown opcode %d", i, (int)I.op);
+      return fail(LVB_ERR_INVALID_ARG, op, buf);
+    }
+    if (I.dst >= LVB_PE_REGS || I.a >= LVB_PE_REGS || I.b >= LVB_PE_REGS) {
+      std::snprintf(buf, sizeof buf, "instruction %d: register above r7", i);
+      return fail(LVB_ERR_INVALID_ARG, op, buf);
+    }
+  }
+  return LVB_OK;
+}
+
 int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e) {
   const char* op = "lvb_gemm_ex";
   int st = lvb_gemm_check(d);
   if (st || !e) return st;
-  const bool any = e->bias || e->residual || e->activation != LVB_ACT_NONE;
+  const bool prog = e->program && e->program->n > 0;
+  const bool any = e->bias || e->residual || e->activation != LVB_ACT_NONE || e->mul || prog;
   if (e->activation < LVB_ACT_NONE || e->activation > LVB_ACT_SILU)
     return fail(LVB_ERR_INVALID_ARG, op, "unknown activation");
   if (any && !float_type(d->c_type))
     return fail(LVB_ERR_UNSUPPORTED, op, "epilogue on an integer output",
-                "coopmat_add and the activations are floating-point");
+                "coopmat_add, coopmat_mul, the activations and per-element programs are "
+                "floating-point; only the clamp modes apply to integer pairs");
   if (e->bias) {
     if (!float_type(e->bias_type))
       return fail(LVB_ERR_UNSUPPORTED, op, "bias type must be Float32, Float16 or BFloat16");
@@ -436,14 +473,40 @@ int lvb_gemm_ex_check(const lvb_gemm_desc* d, const lvb_epilogue* e) {
     if ((uintptr_t)e->bias % dtype_size(e->bias_type))
       return fail(LVB_ERR_INVALID_ARG, op, "bias not aligned to its element size");
   }
-  if (e->residual) {
-    if (!float_type(e->residual_type))
-      return fail(LVB_ERR_UNSUPPORTED, op, "residual type must be Float32, Float16 or BFloat16");
-    const int64_t rmin = std::max<int64_t>(1, d->c_rowmajor ? d->N : d->M);
-    if (e->ldr < rmin)
-      return fail(LVB_ERR_INVALID_ARG, op, d->c_rowmajor ? "ldr < N" : "ldr < M");
-    if ((uintptr_t)e->residual % dtype_size(e->residual_type))
-      return fail(LVB_ERR_INVALID_ARG, op, "residual not aligned to its element size");
+  if (e->residual && (st = check_cmatrix(op, d, e->residual, e->residual_type, e->ldr, "residual", "ldr")))
+    return st;
+  if (e->mul && (st = check_cmatrix(op, d, e->mul, e->mul_type, e->ldm, "mul (coopmat_mul operand)", "ldm")))
+    return st;
+  if (e->program && (st = lvb_pe_program_check(e->program))) return st;
+  if (e->extra) {
+    if (!prog)
+      return fail(LVB_ERR_INVALID_ARG, op, "extra matrix without a per-element program");
+    if ((st = check_cmatrix(op, d, e->extra, e->extra_type, e->lde, "extra (program operand)", "lde")))
+      return st;
+  }
+  if (e->k_pad != 0 && e->k_pad != d->K) {
+    if (e->k_pad < d->K)
+      return fail(LVB_ERR_INVALID_ARG, op, "k_pad < K", "k_pad is the padded k extent, >= K (0: none)");
+    if (e->k_pad > INT32_MAX) return fail(LVB_ERR_UNSUPPORTED, op, "k_pad above 2^31-1");
+    const bool integer = d->a_type == LVB_I8 || d->a_type == LVB_U8;
+    const int modes[2] = {e->a_clamp, e->b_clamp};
+    const double vals[2] = {e->a_clamp_value, e->b_clamp_value};
+    for (int i = 0; i < 2; ++i) {
+      const char* who = i ? "b_clamp" : "a_clamp";
+      if (modes[i] < LVB_CLAMP_UNDEFINED || modes[i] > LVB_CLAMP_TO_EDGE)
+        return fail(LVB_ERR_INVALID_ARG, op, std::string(who) + ": unknown clamp mode");
+      if (modes[i] == LVB_CLAMP_TO_EDGE && d->K == 0)
+        return fail(LVB_ERR_INVALID_ARG, op, std::string(who) + ": TO_EDGE with K == 0",
+                    "an empty operand has no edge element");
+      if (modes[i] == LVB_CLAMP_CONSTANT && integer) {
+        const double lo = d->a_type == LVB_I8 ? -128 : 0, hi = d->a_type == LVB_I8 ? 127 : 255;
+        if (vals[i] != (double)(long long)vals[i] || vals[i] < lo || vals[i] > hi)
+          return fail(LVB_ERR_INVALID_ARG, op,
+                      std::string(who) + ": the clamp value of an 8-bit operand is an integer in its range");
+      }
+    }
+    if (d->K == 0 && !float_type(d->c_type))
+      return fail(LVB_ERR_UNSUPPORTED, op, "k_pad with K == 0 on an integer output");
   }
   return LVB_OK;
 }
@@ -456,14 +519,15 @@ int lvb_gemm_plan_for(const lvb_gemm_desc* d, int32_t sm_count, lvb_gemm_plan* o
 }  // extern "C"
 namespace lvb {
 // c_tma_ok: C's base (when known) and leading dimension allow TMA stores.
-int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out) {
+int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out,
+                bool allow_gemv) {
   int st = lvb_gemm_check(d);
   if (st) return st;
   if (!out) return fail(LVB_ERR_INVALID_ARG, "lvb_gemm", "plan is NULL");
   if (sm_count <= 0) sm_count = 148;
   std::memset(out, 0, sizeof *out);
   if (d->M == 0 || d->N == 0) return LVB_OK;   // nothing to launch
-  if (gemv_applies(d)) {
+  if (allow_gemv && gemv_applies(d)) {
     GemvPlan g;
     gemv_plan(d, sm_count, &g);
     out->gemv = 1;
@@ -549,13 +613,19 @@ static int gemm_enqueue(const char* op, const lvb_gemm_desc* d, const lvb_epilog
   DeviceState* dev = current_device_state(op);
   if (!dev) return LVB_ERR_NO_DEVICE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool epi = e && (e->bias || e->residual || e->activation != LVB_ACT_NONE);
+  const bool prog = e && e->program && e->program->n > 0;
+  const bool clamp = e && e->k_pad > d->K;
+  const bool epi = e && (e->bias || e->residual || e->activation != LVB_ACT_NONE || e->mul ||
+                         prog || clamp);
   if (d->K == 0) return epi ? gemm_epilogue_only(d, e, C, s) : gemm_zero_fill(d, C, s);
-  if (gemv_applies(d)) return gemv_launch(d, epi ? e : nullptr, A, B, C, s, dev);
+  // The matrix-vector kernel carries bias, residual and activation; coopmat_mul, programs and
+  // clamped k tails run on the tensor-core kernel at any shape.
+  if (gemv_applies(d) && !(e && (e->mul || prog || clamp)))
+    return gemv_launch(d, epi ? e : nullptr, A, B, C, s, dev);
   lvb_gemm_plan plan;
   const bool c_tma_ok =
       (uintptr_t)C % 16 == 0 && (d->ldc * dtype_size(d->c_type)) % 16 == 0;
-  int st = gemm_plan_c(d, dev->sm_count, c_tma_ok, &plan);
+  int st = gemm_plan_c(d, dev->sm_count, c_tma_ok, &plan, /*allow_gemv=*/false);
   if (st) return st;
   if (((uintptr_t)A) % 16) plan.repack_a = 1, plan.a_mnmajor = 0;
   if (((uintptr_t)B) % 16) plan.repack_b = 1, plan.b_mnmajor = 0;

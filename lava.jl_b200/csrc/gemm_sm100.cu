@@ -66,6 +66,28 @@ struct GemmParams {
   const void* res;        // nullable; R[m + n*ldr], may be D itself
   int res_kind;
   long long ldr;
+  // coopmat_mul operand S and the per-element program's matrix operand E, both M×N in D's
+  // layout (kernel space, like R); the program runs when prog.n > 0.
+  const void* mul;
+  int mul_kind;
+  long long ldm;
+  const void* ext;
+  int ext_kind;
+  long long lde;
+  int prog_swap;          // 1: the caller's row is kernel n (the product runs as Cᵀ = BᵀAᵀ)
+  PeProgram prog;
+  // Clamped k tail over the padded extent: acc += kx · u[m] · v[n], with u the value kernel A
+  // reads past its last column (row m) and v the one kernel B reads (row n).
+  int kx;                 // k_pad - K (0: none)
+  int cu_mode, cv_mode;   // 1: the clamp constant, 2: the row's element K-1 (to edge)
+  float cu_f, cv_f;       // constants for 16-bit operands
+  int cu_i, cv_i;         // constants for 8-bit operands
+  const void* cu_ptr;     // kernel A / B and their layout, for the edge elements
+  long long cu_ld;
+  int cu_mn;
+  const void* cv_ptr;
+  long long cv_ld;
+  int cv_mn;
   DevStatus* status;
   unsigned long long timeout_ns;
 };
@@ -124,7 +146,55 @@ __device__ __forceinline__ float epi_value(const GemmParams& p, float acc, int m
   float init = bias_m;
   if (p.bias && !p.bias_on_m) init += load_as_f32(p.bias, p.bias_kind, n);
   if (p.res) init += load_as_f32(p.res, p.res_kind, (long long)n * p.ldr + m);
-  return act_any(p.act, acc + init);
+  if (p.kx) init += (float)p.kx * p.cu_f * p.cv_f;   // K == 0: constant clamps only
+  float x = acc + init;
+  if (p.mul) x *= load_as_f32(p.mul, p.mul_kind, (long long)n * p.ldm + m);
+  x = act_any(p.act, x);
+  if (p.prog.n) {
+    float xs[1] = {x};
+    const int rows[1] = {p.prog_swap ? n : m}, cols[1] = {p.prog_swap ? m : n};
+    const float es[1] = {p.ext ? load_as_f32(p.ext, p.ext_kind, (long long)n * p.lde + m) : 0.f};
+    pe_run<1>(p.prog, xs, rows, cols, es);
+    x = xs[0];
+  }
+  return x;
+}
+
+// The clamp term's per-row value u (kernel A's read past column K-1 of row m) and per-column
+// values v (kernel B's, rows n0..n0+nv-1), as fp32 for 16-bit operands.
+template <int AB>
+__device__ __forceinline__ float clamp_u_f(const GemmParams& p, int m) {
+  if (p.cu_mode == 1) return p.cu_f;
+  const long long i = p.cu_mn ? (long long)(p.K - 1) * p.cu_ld + m : (long long)m * p.cu_ld + p.K - 1;
+  return operand_f32(p.cu_ptr, AB, i);
+}
+template <int AB>
+__device__ __forceinline__ float clamp_v_f(const GemmParams& p, int n) {
+  if (p.cv_mode == 1) return p.cv_f;
+  const long long i = p.cv_mn ? (long long)(p.K - 1) * p.cv_ld + n : (long long)n * p.cv_ld + p.K - 1;
+  return operand_f32(p.cv_ptr, AB, i);
+}
+template <int AB>
+__device__ __forceinline__ int clamp_u_i(const GemmParams& p, int m) {
+  if (p.cu_mode == 1) return p.cu_i;
+  const long long i = p.cu_mn ? (long long)(p.K - 1) * p.cu_ld + m : (long long)m * p.cu_ld + p.K - 1;
+  return operand_i32(p.cu_ptr, AB, i);
+}
+template <int AB>
+__device__ __forceinline__ int clamp_v_i(const GemmParams& p, int n) {
+  if (p.cv_mode == 1) return p.cv_i;
+  const long long i = p.cv_mn ? (long long)(p.K - 1) * p.cv_ld + n : (long long)n * p.cv_ld + p.K - 1;
+  return operand_i32(p.cv_ptr, AB, i);
+}
+
+// 8 elements of an M×N operand in D's layout at row m, columns n0..n0+7 (nv of them inside).
+__device__ __forceinline__ void load8(const GemmParams& p, int kind, const void* base,
+                                      long long ld, int m, int n0, int nv, float (&out)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const long long i = p.d_nmajor ? (long long)m * ld + n0 + e : (long long)(n0 + e) * ld + m;
+    out[e] = e < nv ? load_as_f32(base, kind, i) : 0.f;
+  }
 }
 
 __device__ __forceinline__ uint64_t policy_for(int mode, bool is_a) {
@@ -202,12 +272,62 @@ __device__ __forceinline__ void act32(uint32_t (&r)[32], const float (&init)[32]
   for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(act_fn<ACT>(__uint_as_float(r[j]) + init[j]));
 }
 
+// x[j] <- f(act(x[j] · S[m, n0+j])) for the 32 columns n0.. of row m (x already holds
+// acc + bias + R): coopmat_mul, the activation and the caller's program, eight columns at a
+// time.
+__device__ __noinline__ void epi_generic(const GemmParams& p, float* x, int m, int n0, int nv) {
+#pragma unroll 1
+  for (int g = 0; g < 4; ++g) {
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = x[8 * g + e];
+    const int nvg = nv - 8 * g;
+    if (p.mul) {
+      float s8[8];
+      load8(p, p.mul_kind, p.mul, p.ldm, m, n0 + 8 * g, nvg, s8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] *= s8[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = act_any(p.act, v[e]);
+    if (p.prog.n) {
+      float e8[8];
+      if (p.ext) {
+        load8(p, p.ext_kind, p.ext, p.lde, m, n0 + 8 * g, nvg, e8);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) e8[e] = 0.f;
+      }
+      int rows[8], cols[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int n = n0 + 8 * g + e;
+        rows[e] = p.prog_swap ? n : m;
+        cols[e] = p.prog_swap ? m : n;
+      }
+      pe_run<8>(p.prog, v, rows, cols, e8);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[8 * g + e] = v[e];
+  }
+}
+
 // The fused epilogue on one tcgen05.ld worth (32 columns n0.. of row m), in place. `nv`
 // columns are inside the matrix (0 for a row past M: nothing is loaded for it).
-template <int OUT>
+template <int OUT, int AB>
 __device__ __forceinline__ void apply_epilogue(const GemmParams& p, uint32_t (&r)[32], int m,
                                                int n0, int nv, float bias_m) {
-  if constexpr (OUT != OUT_I32) {
+  if constexpr (OUT == OUT_I32) {
+    // Integer outputs take only the clamp term, in wrapping int32 like the accumulation.
+    if (p.kx && nv) {
+      const int u = clamp_u_i<AB>(p, m);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int v = j < nv ? clamp_v_i<AB>(p, n0 + j) : 0;
+        r[j] = (uint32_t)((int)r[j] + (int)((unsigned)p.kx * (unsigned)u * (unsigned)v));
+      }
+    }
+  } else {
     float init[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) init[j] = bias_m;
@@ -218,13 +338,30 @@ __device__ __forceinline__ void apply_epilogue(const GemmParams& p, uint32_t (&r
       else
         add_loaded32(p.res_kind, p.res, (long long)n0 * p.ldr + m, p.ldr, nv, init);
     }
-    switch (p.act) {
-      case LVB_ACT_RELU: act32<LVB_ACT_RELU>(r, init); break;
-      case LVB_ACT_GELU_TANH: act32<LVB_ACT_GELU_TANH>(r, init); break;
-      case LVB_ACT_GELU_ERF: act32<LVB_ACT_GELU_ERF>(r, init); break;
-      case LVB_ACT_SILU: act32<LVB_ACT_SILU>(r, init); break;
-      default: act32<LVB_ACT_NONE>(r, init); break;
+    if (p.kx && nv) {
+      const float u = (float)p.kx * clamp_u_f<AB>(p, m);
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) init[j] = fmaf(u, clamp_v_f<AB>(p, n0 + j), init[j]);
     }
+    if (!p.mul && !p.prog.n) {
+      switch (p.act) {
+        case LVB_ACT_RELU: act32<LVB_ACT_RELU>(r, init); break;
+        case LVB_ACT_GELU_TANH: act32<LVB_ACT_GELU_TANH>(r, init); break;
+        case LVB_ACT_GELU_ERF: act32<LVB_ACT_GELU_ERF>(r, init); break;
+        case LVB_ACT_SILU: act32<LVB_ACT_SILU>(r, init); break;
+        default: act32<LVB_ACT_NONE>(r, init); break;
+      }
+      return;
+    }
+    // coopmat_mul and / or the caller's per-element program, out of line: the values go
+    // through a local array so the common path above keeps its registers.
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]) + init[j];
+    epi_generic(p, x, m, n0, nv);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(x[j]);
   }
 }
 
@@ -331,7 +468,7 @@ __device__ __forceinline__ void commit_pair16(const CUtensorMap* tmD, uint32_t s
 // tcgen05.ld of chunk c+1 is in flight while chunk c goes through the epilogue and its
 // stores, so the TMEM round trip is hidden. `release` hands the accumulator back as soon as
 // every chunk is in registers.
-template <int OUT, int NCH, typename Release>
+template <int OUT, int AB, int NCH, typename Release>
 __device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap* tmD,
                                           uint32_t t_row, int m, int m0w, int n_base,
                                           float bias_m, uint32_t s_out, uint32_t& n_staged,
@@ -342,7 +479,7 @@ __device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap
   uint32_t ra[32], rb[32];
   auto handle = [&](uint32_t (&r)[32], int c) {
     const int n0 = n_base + c * 32;
-    if (p.epi) apply_epilogue<OUT>(p, r, m, n0, m_ok ? min(32, p.N - n0) : 0, bias_m);
+    if (p.epi) apply_epilogue<OUT, AB>(p, r, m, n0, m_ok ? min(32, p.N - n0) : 0, bias_m);
     if constexpr (k16) {
       // 16-bit outputs go out as 32 x 64 boxes: chunk c (even) and c + 1 share one store
       const int np = n_base + (c & ~1) * 32;
@@ -387,7 +524,7 @@ __device__ __forceinline__ uint64_t stage_desc(uint32_t saddr, int mn_major) {
 template <int AB, int OUT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmD, const __grid_constant__ GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
@@ -545,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float bias_m =
           (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * BN;
-      drain_acc<OUT, BN / 32>(p, &tmD, t_row, m, tm * kBM + ew * 32, tn * BN, bias_m, s_out,
+      drain_acc<OUT, AB, BN / 32>(p, &tmD, t_row, m, tm * kBM + ew * 32, tn * BN, bias_m, s_out,
                               n_staged, [&] {
                                 tc_fence_before();
                                 bar_arrive(&tempty[acc]);  // accumulator fully read
@@ -580,7 +717,7 @@ constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + kStoreBytes + 256
 template <int AB, int OUT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ GemmParams p) {
   constexpr int S = kPairStages;
   constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
   constexpr int kElemsPerRow = kInt ? 128 : 64;
@@ -749,7 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float bias_m =
           (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
       const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * 256;
-      drain_acc<OUT, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out, n_staged, [&] {
+      drain_acc<OUT, AB, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out, n_staged, [&] {
         tc_fence_before();
         __syncwarp();
         // TMEM read (tcgen05.wait::ld) and fenced: a relaxed arrive suffices, and skips the
@@ -982,7 +1119,7 @@ static int repack(const void* src, int esize, long long rows, long long cols, lo
 // K == 0 with an epilogue: the accumulator is its initial value bias + R, then the
 // activation, converted and stored (kernel space, like the GEMM's own epilogue).
 template <int OUT>
-__global__ void gemm_epilogue_only_kernel(const GemmParams p) {
+__global__ void gemm_epilogue_only_kernel(const __grid_constant__ GemmParams p) {
   const long long total = (long long)p.M * p.N;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -1244,10 +1381,19 @@ namespace lvb {
 static void set_epilogue(GemmParams& p, const lvb_epilogue* e, bool swap_ab) {
   p.epi = 0;
   p.act = LVB_ACT_NONE;
-  p.bias = p.res = nullptr;
-  p.bias_kind = p.res_kind = LVB_F32;
+  p.bias = p.res = p.mul = p.ext = nullptr;
+  p.bias_kind = p.res_kind = p.mul_kind = p.ext_kind = LVB_F32;
   p.bias_on_m = 0;
-  p.ldr = 0;
+  p.ldr = p.ldm = p.lde = 0;
+  p.prog_swap = swap_ab ? 1 : 0;
+  p.prog.n = 0;
+  p.kx = 0;
+  p.cu_mode = p.cv_mode = 0;
+  p.cu_f = p.cv_f = 0.f;
+  p.cu_i = p.cv_i = 0;
+  p.cu_ptr = p.cv_ptr = nullptr;
+  p.cu_ld = p.cv_ld = 0;
+  p.cu_mn = p.cv_mn = 0;
   if (!e) return;
   p.act = e->activation;
   p.bias = e->bias;
@@ -1256,7 +1402,58 @@ static void set_epilogue(GemmParams& p, const lvb_epilogue* e, bool swap_ab) {
   p.res = e->residual;
   p.res_kind = e->residual_type;
   p.ldr = e->ldr;
-  p.epi = (p.act != LVB_ACT_NONE || p.bias || p.res) ? 1 : 0;
+  p.mul = e->mul;
+  p.mul_kind = e->mul_type;
+  p.ldm = e->ldm;
+  if (e->program && e->program->n > 0) {
+    p.prog.n = e->program->n;
+    std::memcpy(p.prog.code, e->program->code, sizeof p.prog.code);
+    p.ext = e->extra;
+    p.ext_kind = e->extra_type;
+    p.lde = e->lde;
+  }
+  p.epi = (p.act != LVB_ACT_NONE || p.bias || p.res || p.mul || p.prog.n) ? 1 : 0;
+}
+
+// The clamp term of the padded k extent (kernel space: kernel A is the caller's B when the
+// product runs as Cᵀ = BᵀAᵀ). `ka`/`kb` are the kernel operands as the kernel reads them.
+static void set_clamp(GemmParams& p, const lvb_epilogue* e, const lvb_gemm_desc* d, bool swap_ab,
+                      const void* ka, long long lda_k, int ka_mn, const void* kb, long long ldb_k,
+                      int kb_mn) {
+  if (!e || e->k_pad <= d->K) return;
+  const int mode_a = swap_ab ? e->b_clamp : e->a_clamp;
+  const int mode_b = swap_ab ? e->a_clamp : e->b_clamp;
+  const double val_a = swap_ab ? e->b_clamp_value : e->a_clamp_value;
+  const double val_b = swap_ab ? e->a_clamp_value : e->b_clamp_value;
+  const bool integer = d->a_type == LVB_I8 || d->a_type == LVB_U8;
+  // the clamp constant as the operand's type reads it (tensor_clampbits): RNE to 16 bits
+  auto as_operand = [&](double v) -> float {
+    if (d->a_type == LVB_F16) return __half2float(__float2half_rn((float)v));
+    return __bfloat162float(__float2bfloat16_rn((float)v));
+  };
+  // a reader of zero (undefined or a zero constant) makes the whole term zero
+  auto zero = [&](int mode, double v) {
+    return mode == LVB_CLAMP_UNDEFINED || (mode == LVB_CLAMP_CONSTANT &&
+                                           (integer ? (long long)v == 0 : as_operand(v) == 0.f));
+  };
+  if (zero(mode_a, val_a) || zero(mode_b, val_b)) return;
+  p.kx = (int)(e->k_pad - d->K);
+  p.cu_mode = mode_a == LVB_CLAMP_TO_EDGE ? 2 : 1;
+  p.cv_mode = mode_b == LVB_CLAMP_TO_EDGE ? 2 : 1;
+  if (integer) {
+    p.cu_i = (int)val_a;
+    p.cv_i = (int)val_b;
+  } else {
+    p.cu_f = as_operand(val_a);
+    p.cv_f = as_operand(val_b);
+  }
+  p.cu_ptr = ka;
+  p.cu_ld = lda_k;
+  p.cu_mn = ka_mn;
+  p.cv_ptr = kb;
+  p.cv_ld = ldb_k;
+  p.cv_mn = kb_mn;
+  p.epi = 1;
 }
 
 int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
@@ -1267,7 +1464,9 @@ int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
   p.N = (int)(swap ? d->M : d->N);
   p.D = C;
   p.ldd = d->ldc;
+  p.K = 0;
   set_epilogue(p, e, swap);
+  set_clamp(p, e, d, swap, nullptr, 0, 0, nullptr, 0, 0);   // K == 0: constants only
   const long long total = (long long)p.M * p.N;
   const int blocks = (int)std::min<long long>((total + 255) / 256, 4096);
   switch (out_kind_of(d->c_type)) {
@@ -1278,6 +1477,81 @@ int gemm_epilogue_only(const lvb_gemm_desc* d, const lvb_epilogue* e, void* C,
   }
   cudaError_t err = cudaGetLastError();
   return err == cudaSuccess ? LVB_OK : fail_cuda(err, "lvb_gemm_ex", "epilogue launch");
+}
+
+// The tensor maps of one call: operands K-major (rows of K elements, boxes of 128 K-bytes ×
+// tile rows) or MN-major (rows of MN elements, one per k, boxes of 64 MN elements × 64 k);
+// the CTA pair stages half of the 256-column B tile per CTA. Kernel-space D is n-contiguous
+// when the plan oriented the product that way (C can take TMA stores): its interior boxes
+// (32 m × 64 n of 16-bit or 32 m × 32 n of 32-bit elements: rows of 128 bytes) then go out
+// through TMA tensor stores with the 128B row swizzle the epilogue writes.
+static int encode_maps(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* kA,
+                       const void* kB, int64_t kM, int64_t kN, int64_t ldka, int64_t ldkb,
+                       int ka_mn, int kb_mn, void* C, int d_nmajor, CUtensorMap* ta,
+                       CUtensorMap* tb, CUtensorMap* td, int* stage_out) {
+  const int esize = dtype_size(d->a_type);
+  const uint32_t box_k = 128 / esize;
+  int st = ka_mn ? make_tmap_2d(ta, kA, esize, (uint64_t)kM, (uint64_t)d->K, (uint64_t)ldka, 64,
+                                64, "lvb_gemm")
+                 : make_tmap_2d(ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka,
+                                box_k, kBM, "lvb_gemm");
+  if (st) return st;
+  st = kb_mn ? make_tmap_2d(tb, kB, esize, (uint64_t)kN, (uint64_t)d->K, (uint64_t)ldkb, 64, 64,
+                            "lvb_gemm")
+             : make_tmap_2d(tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
+                            plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
+  if (st) return st;
+  const int osize = dtype_size(d->c_type);
+  std::memset(td, 0, sizeof *td);
+  *stage_out = 0;
+  if (d_nmajor) {
+    if (make_tmap_2d_sw(td, C, osize, (uint64_t)kN, (uint64_t)kM, (uint64_t)d->ldc,
+                        osize == 2 ? 64 : 32, 32, 128, "lvb_gemm") == LVB_OK)
+      *stage_out = 1;
+    else
+      clear_error();   // direct stores in the same orientation: correct, slower
+  }
+  return LVB_OK;
+}
+
+// A few recent calls' tensor maps per host thread (no lock: thread-local), compared byte for
+// byte on everything the maps are encoded from.
+struct MapKey {
+  int device;
+  int swap, pair, tile_n, a_mn, b_mn;
+  lvb_gemm_desc d;
+  const void* A;
+  const void* B;
+  void* C;
+};
+struct MapVal {
+  CUtensorMap ta, tb, td;
+  int stage_out;
+};
+constexpr int kMapCacheSize = 8;
+struct MapCache {
+  MapKey key[kMapCacheSize];
+  MapVal val[kMapCacheSize];
+  int used = 0, next = 0;
+};
+static thread_local MapCache t_maps;
+
+static const MapVal* map_cache_find(const MapKey& k) {
+  for (int i = 0; i < t_maps.used; ++i)
+    if (std::memcmp(&t_maps.key[i], &k, sizeof k) == 0) return &t_maps.val[i];
+  return nullptr;
+}
+
+static void map_cache_insert(const MapKey& k, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const CUtensorMap& td, int stage_out) {
+  const int i = t_maps.next;
+  t_maps.key[i] = k;
+  t_maps.val[i].ta = ta;
+  t_maps.val[i].tb = tb;
+  t_maps.val[i].td = td;
+  t_maps.val[i].stage_out = stage_out;
+  t_maps.next = (i + 1) % kMapCacheSize;
+  if (t_maps.used < kMapCacheSize) ++t_maps.used;
 }
 
 int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,
@@ -1296,35 +1570,34 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   const int kb_mn = plan.swap_ab ? plan.a_mnmajor : plan.b_mnmajor;
   const uint32_t box_k = 128 / esize;
 
-  CUtensorMap ta, tb;
-  // K-major: rows of K elements, boxes of 128 K-bytes × tile rows. MN-major: rows of MN
-  // elements (one per k), boxes of 64 MN elements × 64 k.
-  int st = ka_mn ? make_tmap_2d(&ta, kA, esize, (uint64_t)kM, (uint64_t)d->K, (uint64_t)ldka, 64,
-                                64, "lvb_gemm")
-                 : make_tmap_2d(&ta, kA, esize, (uint64_t)d->K, (uint64_t)kM, (uint64_t)ldka,
-                                box_k, kBM, "lvb_gemm");
-  if (st) return st;
-  // The CTA pair stages half of the 256-column B tile per CTA.
-  st = kb_mn ? make_tmap_2d(&tb, kB, esize, (uint64_t)kN, (uint64_t)d->K, (uint64_t)ldkb, 64, 64,
-                            "lvb_gemm")
-             : make_tmap_2d(&tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
-                            plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
-  if (st) return st;
-  // Kernel-space D is n-contiguous when the plan oriented the product that way (C can take
-  // TMA stores); its interior boxes (32 m × 64 n of 16-bit or 32 m × 32 n of 32-bit
-  // elements: rows of 128 bytes) then go out through TMA tensor stores with the 128B row
-  // swizzle the epilogue writes.
-  const int osize = dtype_size(d->c_type);
   const int d_nmajor = (plan.swap_ab != 0) != (d->c_rowmajor != 0);
-  CUtensorMap td;
-  std::memset(&td, 0, sizeof td);
+  CUtensorMap ta, tb, td;
   int stage_out = 0;
-  if (d_nmajor) {
-    if (make_tmap_2d_sw(&td, C, osize, (uint64_t)kN, (uint64_t)kM, (uint64_t)d->ldc,
-                        osize == 2 ? 64 : 32, 32, 128, "lvb_gemm") == LVB_OK)
-      stage_out = 1;
-    else
-      clear_error();   // direct stores in the same orientation: correct, slower
+  // The three tensor maps depend only on the descriptor, the plan's orientation and tiles and
+  // the three pointers: a call repeating a recent one on this thread reuses them (encoding
+  // them is most of the host time of a small GEMM).
+  MapKey key;
+  std::memset(&key, 0, sizeof key);
+  key.device = dev->device;
+  key.d = *d;
+  key.A = A;
+  key.B = B;
+  key.C = C;
+  key.swap = plan.swap_ab;
+  key.pair = plan.cta_pair;
+  key.tile_n = plan.tile_n;
+  key.a_mn = ka_mn;
+  key.b_mn = kb_mn;
+  if (const MapVal* hit = map_cache_find(key)) {
+    ta = hit->ta;
+    tb = hit->tb;
+    td = hit->td;
+    stage_out = hit->stage_out;
+  } else {
+    const int st = encode_maps(d, plan, kA, kB, kM, kN, ldka, ldkb, ka_mn, kb_mn, C, d_nmajor,
+                               &ta, &tb, &td, &stage_out);
+    if (st) return st;
+    map_cache_insert(key, ta, tb, td, stage_out);
   }
 
   GemmParams p;
@@ -1333,6 +1606,7 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
   p.d_nmajor = d_nmajor;
   p.stage_out = stage_out;
   set_epilogue(p, epi, plan.swap_ab != 0);
+  set_clamp(p, epi, d, plan.swap_ab != 0, kA, ldka, ka_mn, kB, ldkb, kb_mn);
   p.M = (int)kM;
   p.N = (int)kN;
   p.K = (int)d->K;

@@ -70,7 +70,10 @@ const char* dtype_name(int dt);
 // ---- GEMM (gemm_sm100.cu) ----
 // lvb_gemm_plan_for with C's TMA-store capability known (its base and leading dimension):
 // it decides the orientation of the product in kernel space.
-int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out);
+// allow_gemv = false plans the tensor-core kernel even for a matrix-vector shape (epilogues
+// the streaming kernel does not carry).
+int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gemm_plan* out,
+                bool allow_gemv = true);
 
 // `epi` is NULL for a plain GEMM.
 int gemm_launch(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const void* A,

@@ -34,6 +34,7 @@ LVB_OK, LVB_ERR_INVALID_ARG, LVB_ERR_UNSUPPORTED, LVB_ERR_CUDA = 0, 1, 2, 3
 LVB_ERR_TIMEOUT, LVB_ERR_NCCL, LVB_ERR_NO_DEVICE = 4, 5, 6
 F16, BF16, F32, I8, U8, I32, U32 = range(7)
 ACT_NONE, ACT_RELU, ACT_GELU_TANH, ACT_GELU_ERF, ACT_SILU = range(5)
+CLAMP_UNDEFINED, CLAMP_CONSTANT, CLAMP_TO_EDGE = range(3)
 ACTIVATIONS = {None: ACT_NONE, "none": ACT_NONE, "relu": ACT_RELU, "gelu": ACT_GELU_TANH,
                "gelu_tanh": ACT_GELU_TANH, "gelu_erf": ACT_GELU_ERF, "silu": ACT_SILU}
 BIAS_PER_ROW, BIAS_PER_COL = 0, 1
@@ -47,7 +48,7 @@ EXPORTS = [
     "lvb_caps_sm100", "lvb_caps", "lvb_matrix_shapes", "lvb_bestshape",
     "lvb_gemm_check", "lvb_gemm_plan_for", "lvb_gemm", "lvb_gemm_noalloc",
     "lvb_gemm_noalloc_status", "lvb_gemm_noalloc_selftest_wait_timeout",
-    "lvb_gemm_ex_check", "lvb_gemm_ex",
+    "lvb_gemm_ex_check", "lvb_gemm_ex", "lvb_pe_program_check",
     "lvb_attention_check", "lvb_attention_plan_for", "lvb_attention_fwd",
     "lvb_abi_version", "lvb_last_error", "lvb_status_string", "lvb_device_count",
     "lvb_set_device", "lvb_malloc", "lvb_free", "lvb_memcpy_htod", "lvb_memcpy_dtoh",
@@ -115,7 +116,12 @@ class lvb_attn_plan(C.Structure):
 class lvb_epilogue(C.Structure):
     _fields_ = [("bias", C.c_void_p), ("residual", C.c_void_p), ("ldr", C.c_int64),
                 ("bias_type", C.c_int32), ("bias_axis", C.c_int32),
-                ("residual_type", C.c_int32), ("activation", C.c_int32)]
+                ("residual_type", C.c_int32), ("activation", C.c_int32),
+                ("mul", C.c_void_p), ("ldm", C.c_int64), ("mul_type", C.c_int32),
+                ("extra_type", C.c_int32), ("extra", C.c_void_p), ("lde", C.c_int64),
+                ("program", C.c_void_p), ("k_pad", C.c_int64),
+                ("a_clamp", C.c_int32), ("b_clamp", C.c_int32),
+                ("a_clamp_value", C.c_double), ("b_clamp_value", C.c_double)]
 
 
 class lvb_attn_desc(C.Structure):
@@ -149,6 +155,7 @@ def _load() -> C.CDLL:
                                      C.POINTER(C.c_int32)], C.c_int),
         "lvb_gemm_noalloc_selftest_wait_timeout": ([C.c_int32, P], C.c_int),
         "lvb_gemm_ex_check": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue)], C.c_int),
+        "lvb_pe_program_check": ([P], C.c_int),
         "lvb_gemm_ex": ([C.POINTER(lvb_gemm_desc), C.POINTER(lvb_epilogue), P, P, P, P], C.c_int),
         "lvb_attention_check": ([C.POINTER(lvb_attn_desc)], C.c_int),
         "lvb_attention_fwd": ([C.POINTER(lvb_attn_desc), P, P, P, P, P, P], C.c_int),
@@ -357,10 +364,37 @@ def _stream_ptr(stream) -> Optional[int]:
     return stream.cuda_stream
 
 
-def epilogue(C_, bias=None, bias_axis: str = "col", residual=None, activation=None) -> lvb_epilogue:
-    """The ``lvb_epilogue`` for ``C = act(A·B + bias + residual)``: ``bias`` a contiguous
-    vector added per column (``bias_axis="col"``, N elements) or per row (``"row"``, M
-    elements); ``residual`` an M×N tensor in C's layout (it may be C itself)."""
+def _cmatrix(C_, t, what):
+    """(pointer, type, leading dimension) of an M×N epilogue operand in C's layout."""
+    if tuple(t.shape) != tuple(C_.shape):
+        raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm_ex: {what} must have C's shape")
+    rm, ld = _layout2d(t, what)
+    crm, _ = _layout2d(C_, "C")
+    if rm != crm and min(C_.shape) > 1:
+        raise LavaError(LVB_ERR_UNSUPPORTED, f"lvb_gemm_ex: {what} must have C's layout")
+    return t.data_ptr(), dtype_of(t), ld
+
+
+def _clamp(spec):
+    """A clamp given as None / "undefined", "edge", or a number (the constant)."""
+    if spec is None or spec == "undefined":
+        return CLAMP_UNDEFINED, 0.0
+    if spec == "edge":
+        return CLAMP_TO_EDGE, 0.0
+    if isinstance(spec, (int, float)) and not isinstance(spec, bool):
+        return CLAMP_CONSTANT, float(spec)
+    raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm_ex: clamp {spec!r}: None, 'edge' or a number")
+
+
+def epilogue(C_, bias=None, bias_axis: str = "col", residual=None, activation=None, mul=None,
+             program=None, extra=None, k_pad=None, a_clamp=None, b_clamp=None) -> lvb_epilogue:
+    """The ``lvb_epilogue`` for ``C = f(act((A·B + bias + residual) ⊙ mul))``: ``bias`` a
+    contiguous vector added per column (``bias_axis="col"``, N elements) or per row (``"row"``,
+    M elements); ``residual`` and ``mul`` M×N tensors in C's layout (the residual may be C
+    itself); ``program`` a ``perelement.Program`` (or a Python function, traced) with
+    ``extra`` its M×N matrix operand; ``k_pad`` the padded k extent whose reads past K take
+    ``a_clamp`` / ``b_clamp`` (None, ``"edge"`` or a constant). The program structure is kept
+    alive on the returned value (``e._keep``) for the duration of the call."""
     e = lvb_epilogue()
     if activation not in ACTIVATIONS:
         raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm_ex: unknown activation {activation!r}")
@@ -376,34 +410,82 @@ def epilogue(C_, bias=None, bias_axis: str = "col", residual=None, activation=No
         e.bias_type = dtype_of(bias)
         e.bias_axis = BIAS_PER_COL if bias_axis == "col" else BIAS_PER_ROW
     if residual is not None:
-        if tuple(residual.shape) != tuple(C_.shape):
-            raise LavaError(LVB_ERR_INVALID_ARG, "lvb_gemm_ex: residual must have C's shape")
-        rrm, ldr = _layout2d(residual, "residual")
-        crm, _ = _layout2d(C_, "C")
-        if rrm != crm and min(C_.shape) > 1:
-            raise LavaError(LVB_ERR_UNSUPPORTED, "lvb_gemm_ex: residual must have C's layout")
-        e.residual = residual.data_ptr()
-        e.residual_type = dtype_of(residual)
-        e.ldr = ldr
+        e.residual, e.residual_type, e.ldr = _cmatrix(C_, residual, "residual")
+    if mul is not None:
+        e.mul, e.mul_type, e.ldm = _cmatrix(C_, mul, "mul")
+    e._keep = None
+    if program is not None:
+        from .perelement import Program, program as trace
+        prog = program if isinstance(program, Program) else trace(program)
+        st = prog.to_struct()
+        e._keep = st
+        e.program = C.addressof(st)
+        if extra is not None:
+            e.extra, e.extra_type, e.lde = _cmatrix(C_, extra, "extra")
+    elif extra is not None:
+        raise LavaError(LVB_ERR_INVALID_ARG, "lvb_gemm_ex: extra without a program")
+    if k_pad is not None:
+        e.k_pad = int(k_pad)
+        e.a_clamp, e.a_clamp_value = _clamp(a_clamp)
+        e.b_clamp, e.b_clamp_value = _clamp(b_clamp)
     return e
 
 
 def gemm(C_, A, B, stream=None, c_type: Optional[int] = None, bias=None, bias_axis="col",
-         residual=None, activation=None):
+         residual=None, activation=None, mul=None, program=None, extra=None, k_pad=None,
+         a_clamp=None, b_clamp=None):
     """``gemm!(C, A, B)``: C = A·B on the GPU (torch CUDA tensors, logical shapes
     (M,K)·(K,N) -> (M,N)); enqueued on ``stream`` (default: torch's current stream).
     ``c_type`` overrides the component type read from C (e.g. U32 held in an int32
-    tensor). With ``bias``, ``residual`` or ``activation`` the fused epilogue runs:
-    C = act(A·B + bias + residual) (``lvb_gemm_ex``)."""
+    tensor). With any of the epilogue keywords the fused epilogue runs (``lvb_gemm_ex``, see
+    ``epilogue``): C = program(act((A·B + bias + residual) ⊙ mul)), the product over
+    ``k_pad`` columns with the clamp modes when given."""
     d = gemm_desc(C_, A, B, c_type)
-    if bias is None and residual is None and activation in (None, "none"):
+    if (bias is None and residual is None and activation in (None, "none") and mul is None
+            and program is None and k_pad is None):
         check(lib.lvb_gemm(C.byref(d), A.data_ptr(), B.data_ptr(), C_.data_ptr(),
                            _stream_ptr(stream)))
         return C_
-    e = epilogue(C_, bias, bias_axis, residual, activation)
+    e = epilogue(C_, bias, bias_axis, residual, activation, mul, program, extra, k_pad,
+                 a_clamp, b_clamp)
     check(lib.lvb_gemm_ex(C.byref(d), C.byref(e), A.data_ptr(), B.data_ptr(), C_.data_ptr(),
                           _stream_ptr(stream)))
     return C_
+
+
+class GemmCall:
+    """A GEMM validated and described once, launched many times: ``g = prepare_gemm(C, A, B,
+    ...)`` then ``g()`` (or ``g(stream)``) enqueues ``lvb_gemm`` / ``lvb_gemm_ex`` with the
+    prepared descriptor — one foreign call per launch, for small problems whose time is the
+    host's. The tensors must stay alive and keep their storage while the object is used."""
+
+    def __init__(self, C_, A, B, c_type=None, **epi):
+        self.d = gemm_desc(C_, A, B, c_type)
+        self.ptrs = (A.data_ptr(), B.data_ptr(), C_.data_ptr())
+        self.keep = (C_, A, B)
+        active = {k: v for k, v in epi.items() if v is not None and v != "none"}
+        self.e = epilogue(C_, **epi) if active else None
+        self._fn = lib.lvb_gemm if self.e is None else lib.lvb_gemm_ex
+        self._d = C.byref(self.d)
+        self._args = ((self._d,) if self.e is None else (self._d, C.byref(self.e))) + self.ptrs
+        self._default_stream = None
+
+    def __call__(self, stream=None):
+        if stream is None:
+            if self._default_stream is None:
+                self._default_stream = _stream_ptr(None)
+            s = self._default_stream
+        else:
+            s = _stream_ptr(stream)
+        st = self._fn(*self._args, s)
+        if st:
+            check(st)
+
+
+def prepare_gemm(C_, A, B, c_type=None, **epi) -> GemmCall:
+    """See ``GemmCall``; keywords as ``gemm``'s epilogue keywords. The default stream is
+    torch's current stream at the first call."""
+    return GemmCall(C_, A, B, c_type, **epi)
 
 
 def gemm_plan(M, N, K, a_type=F16, c_type=F32, c_rowmajor=False, sm_count=148,

@@ -164,3 +164,62 @@ def gemm_epilogue_ref(A: np.ndarray, B: np.ndarray, out: str, bias=None, bias_ax
     pre = A.astype(np.float64) @ B.astype(np.float64) + init
     val = ACTIVATIONS[act](pre)
     return coopmat_convert(val, out) if rounded else val
+
+
+# ---- clamped loads over a padded k extent, coopmat_mul and per-element programs ---------
+def clamp_pad(X: np.ndarray, k_pad: int, axis: int, mode: str, value, T: str) -> np.ndarray:
+    """``X`` (values of type T) extended along ``axis`` (its k axis) to ``k_pad`` entries, as
+    a load through a tensor layout with clamp ``mode`` reads past the extent
+    (src/vocabulary/tensor.jl:46-51; src/device/tensor_intrinsics.jl:139-148):
+    "undefined" -> 0 (this library's choice), "constant" -> ``value`` in T's bits
+    (tensor_clampbits, tensor.jl:83-85: rounded to the component type), "edge" -> the nearest
+    element inside (index K-1)."""
+    K = X.shape[axis]
+    extra = k_pad - K
+    if extra <= 0:
+        return X
+    shape = list(X.shape)
+    shape[axis] = extra
+    if mode == "edge":
+        edge = np.take(X, [K - 1], axis=axis)
+        pad = np.repeat(edge, extra, axis=axis)
+    elif mode == "constant":
+        if np.issubdtype(X.dtype, np.integer):
+            v = int(value)
+        else:
+            v = coopmat_convert(np.array([float(value)]), T)[0] if T != "Float32" else float(value)
+        pad = np.full(shape, v, dtype=X.dtype)
+    else:
+        pad = np.zeros(shape, dtype=X.dtype)
+    return np.concatenate([X, pad], axis=axis)
+
+
+def gemm_vocab_ref(A: np.ndarray, B: np.ndarray, out: str, T: str, bias=None,
+                   bias_axis: str = "col", residual=None, act=None, mul=None, program=None,
+                   extra=None, k_pad=None, a_clamp=("undefined", 0), b_clamp=("undefined", 0),
+                   rounded: bool = True):
+    """The fused GEMM with every epilogue step, as a Lava kernel would compose them:
+    acc = coopmat_add(bias, residual) as the initial accumulator, muladd over the k extent
+    (``k_pad`` columns with the clamped reads, float64 here), then coopmat_mul by ``mul``
+    (coopmat_intrinsics.jl:402-464), the activation, the per-element ``program`` on fp32
+    values with 0-based row/col and the ``extra`` matrix's element (oracle/perelement.py), and
+    one conversion to ``out``. Integer pairs: the exact int64 product of the padded operands
+    (the clamp modes are their only epilogue)."""
+    M, N = A.shape[0], B.shape[1]
+    if k_pad is not None and k_pad > A.shape[1]:
+        A = clamp_pad(A, k_pad, 1, a_clamp[0], a_clamp[1], T)
+        B = clamp_pad(B, k_pad, 0, b_clamp[0], b_clamp[1], T)
+    if np.issubdtype(A.dtype, np.integer):
+        return gemm_ref(A, B, out)
+    init = epilogue_init(M, N, bias, bias_axis, residual).astype(np.float64)
+    v = A.astype(np.float64) @ B.astype(np.float64) + init
+    if mul is not None:
+        v = v * np.asarray(mul, dtype=np.float64)
+    v = ACTIVATIONS[act](v)
+    if program is not None:
+        from .perelement import pe_eval
+        rows = np.arange(M)[:, None] * np.ones((1, N), dtype=np.int64)
+        cols = np.ones((M, 1), dtype=np.int64) * np.arange(N)[None, :]
+        ext = None if extra is None else np.asarray(extra, dtype=np.float32)
+        v = pe_eval(program, v.astype(np.float32), rows, cols, ext).astype(np.float64)
+    return coopmat_convert(v, out) if rounded else v

@@ -59,7 +59,7 @@ def test_struct_layouts_match_header(lvb, tmp_path):
 def test_library_needs_no_libcuda_at_load(lvb):
     out = subprocess.run(["ldd", str(lvb.LIB_PATH)], capture_output=True, text=True).stdout
     assert "libcuda.so" not in out
-    assert lvb.abi_version() == 4
+    assert lvb.abi_version() == 5
 
 
 def test_static_caps_answer(lvb):

@@ -251,13 +251,13 @@ def band_rows(M, bands, seed, band=256):
 
 @pytest.mark.slow
 def test_config2_fp16_8192_sampled_rows_and_row_checksums(lvb, torch_cuda):
-    """C2 at full size: 130 sampled rows (both edges of 64 tile bands) checked element by
+    """C2 at full size: 130 sampled rows (both edges of 64 128-row tile bands) checked element by
     element against the float64 oracle, and every row through its checksum."""
     torch = torch_cuda
     cfg = GEMM_CONFIGS["C2"]
     A, Bt = gemm_inputs(cfg["M"], cfg["N"], cfg["K"], cfg["ab"], cfg["seed"])
     C = run(lvb, torch, A, Bt, "Float16", "Float16", c_rowmajor=True)
-    rows = band_rows(cfg["M"], 64, seed=0)
+    rows = band_rows(cfg["M"], 64, seed=0, band=128)
     assert len(rows) >= 128
     check(C[rows], A[rows], Bt.T, "Float16")
     colsum = Bt.astype(np.float64).sum(axis=0)
