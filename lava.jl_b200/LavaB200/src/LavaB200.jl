@@ -34,6 +34,7 @@ using LinearAlgebra: Transpose, transpose
 import KernelInterface as KI
 
 export B200Backend, B200Array, gemm!, attention!, device_status, caps_raw, matrix_shapes_raw,
+       pe_program, PeProgram,
        LavaB200Error, BFloat16, shard_range, comm_unique_id, Comm, allgather!
 
 const libpath = Ref{String}("")
@@ -119,7 +120,21 @@ struct Epilogue
     bias::Ptr{Cvoid}; residual::Ptr{Cvoid}
     ldr::Int64
     bias_type::Int32; bias_axis::Int32; residual_type::Int32; activation::Int32
+    mul::Ptr{Cvoid}; ldm::Int64; mul_type::Int32; extra_type::Int32
+    extra::Ptr{Cvoid}; lde::Int64
+    program::Ptr{Cvoid}; k_pad::Int64
+    a_clamp::Int32; b_clamp::Int32
+    a_clamp_value::Float64; b_clamp_value::Float64
 end
+
+# tensor clamp modes (src/vocabulary/tensor.jl:46-51) as `gemm!` takes them
+const CLAMPS = Dict{Symbol,Int32}(:undefined => 0, :constant => 1, :edge => 2)
+clampspec(::Nothing) = (Int32(0), 0.0)
+clampspec(s::Symbol) = s === :edge ? (Int32(2), 0.0) :
+    s === :undefined ? (Int32(0), 0.0) : throw(ArgumentError("clamp: :edge, :undefined or a number"))
+clampspec(v::Real) = (Int32(1), Float64(v))
+
+include("perelement.jl")
 
 const ACTIVATIONS = Dict{Symbol,Int32}(:none => 0, :relu => 1, :gelu => 2, :gelu_tanh => 2,
                                        :gelu_erf => 3, :silu => 4)
@@ -236,7 +251,8 @@ elt(x::Transpose) = eltype(parent(x))
 
 """
     gemm!(C, A, B; bias = nothing, bias_axis = :row, residual = nothing, activation = :none,
-          stream = C_NULL) -> C
+          mul = nothing, perelement = nothing, extra = nothing, k_pad = nothing,
+          a_clamp = nothing, b_clamp = nothing, stream = C_NULL) -> C
 
 `C = activation(A·B + bias + residual)` on the GPU. Any layout: a plain device matrix is
 column-major, its `transpose` row-major (Lava's `Val(true)` load); A column-major / B row-major
@@ -249,20 +265,33 @@ matrix in C's layout (may be `C` itself); `activation` one of `:none, :relu, :ge
 residual)` and finished with `coopmat_perelement` (src/device/coopmat_intrinsics.jl:
 435-447,551-593). Floating-point outputs only.
 
+More of the vocabulary on the same epilogue: `mul` an M×N matrix in C's layout multiplying
+the accumulator element-wise (`coopmat_mul`, src/device/coopmat_intrinsics.jl:402-464);
+`perelement` a function `(x, row, col, e) -> value` applied to every element with its 0-based
+row and column and the element `e` of the optional matrix `extra` (`coopmat_perelement`,
+coopmat_intrinsics.jl:520-678), traced once into the library's per-element program
+(`pe_program`); `k_pad` a padded k extent whose reads past `K` take `a_clamp` / `b_clamp`
+(`nothing`, `:edge` or a constant: TENSOR_CLAMP_TO_EDGE / TENSOR_CLAMP_CONSTANT,
+src/vocabulary/tensor.jl:46-51). The result is
+`perelement(activation((A·B + bias + residual) .* mul))`.
+
 A device vector as `B` and `C` (N == 1), or a 1×K `A` (M == 1), is a matrix-vector product:
 it runs on the library's HBM-bound streaming kernel — `dot4x8` for Int8/UInt8 operands
 (src/vocabulary/vocabulary.jl:18-35), fp32 multiply-adds for Float16/BFloat16 — with the
 same results and epilogue.
 """
 function gemm!(C, A, B; bias = nothing, bias_axis::Symbol = :row, residual = nothing,
-               activation::Symbol = :none, stream::Ptr{Cvoid} = C_NULL)
+               activation::Symbol = :none, mul = nothing, perelement = nothing,
+               extra = nothing, k_pad = nothing, a_clamp = nothing, b_clamp = nothing,
+               stream::Ptr{Cvoid} = C_NULL)
     pa, M, K, ra, lda = layout(A)
     pb, K2, N, rb, ldb = layout(B)
     pc, M2, N2, rc, ldc = layout(C)
     (K2 == K && M2 == M && N2 == N) ||
         throw(DimensionMismatch("gemm!: ($M×$K)·($K2×$N) -> ($M2×$N2)"))
     d = GemmDesc(dtype(elt(A)), dtype(elt(B)), dtype(elt(C)), ra, rb, rc, M, N, K, lda, ldb, ldc)
-    if bias === nothing && residual === nothing && activation === :none
+    if bias === nothing && residual === nothing && activation === :none && mul === nothing &&
+       perelement === nothing && k_pad === nothing
         check(ccall(sym(:lvb_gemm), Cint,
                     (Ref{GemmDesc}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
                     d, pa, pb, pc, stream))
@@ -277,18 +306,32 @@ function gemm!(C, A, B; bias = nothing, bias_axis::Symbol = :row, residual = not
             throw(DimensionMismatch("gemm!: bias of length $(length(bias)) for $bias_axis of ($M×$N)"))
         pbias, tbias = pointer(bias), dtype(eltype(bias))
     end
-    pres, tres, ldr = C_NULL, Int32(2), Int64(0)
-    if residual !== nothing
-        pr, Mr, Nr, rr, ldr_ = layout(residual)
-        (Mr == M && Nr == N && rr == rc) ||
-            throw(DimensionMismatch("gemm!: residual must be ($M×$N) in C's layout"))
-        pres, tres, ldr = pr, dtype(elt(residual)), Int64(ldr_)
+    # an M×N epilogue operand in C's layout: (pointer, type, leading dimension)
+    function cmatrix(x, what)
+        px, Mx, Nx, rx, ldx = layout(x)
+        (Mx == M && Nx == N && rx == rc) ||
+            throw(DimensionMismatch("gemm!: $what must be ($M×$N) in C's layout"))
+        return Ptr{Cvoid}(px), dtype(elt(x)), Int64(ldx)
     end
-    e = Epilogue(pbias, pres, ldr, tbias, Int32(bias_axis === :row ? 0 : 1), tres,
-                 ACTIVATIONS[activation])
-    check(ccall(sym(:lvb_gemm_ex), Cint,
-                (Ref{GemmDesc}, Ref{Epilogue}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
-                d, e, pa, pb, pc, stream))
+    pres, tres, ldr = residual === nothing ? (C_NULL, Int32(2), Int64(0)) : cmatrix(residual, "residual")
+    pmul, tmul, ldm = mul === nothing ? (C_NULL, Int32(2), Int64(0)) : cmatrix(mul, "mul")
+    prog = perelement === nothing ? nothing :
+           perelement isa PeProgram ? perelement : pe_program(perelement)
+    pext, text, lde = extra === nothing ? (C_NULL, Int32(2), Int64(0)) : cmatrix(extra, "extra")
+    (extra === nothing || prog !== nothing) ||
+        throw(ArgumentError("gemm!: extra is the perelement function's matrix operand"))
+    ca, va = clampspec(a_clamp)
+    cb, vb = clampspec(b_clamp)
+    progref = Ref(prog === nothing ? PeProgram(Int32(0), ntuple(_ -> PeInstr(0, 0, 0, 0, 0), 32)) : prog)
+    GC.@preserve progref begin
+        pprog = prog === nothing ? C_NULL : Ptr{Cvoid}(Base.unsafe_convert(Ptr{PeProgram}, progref))
+        e = Epilogue(pbias, pres, ldr, tbias, Int32(bias_axis === :row ? 0 : 1), tres,
+                     ACTIVATIONS[activation], pmul, ldm, tmul, text, pext, lde, pprog,
+                     k_pad === nothing ? Int64(0) : Int64(k_pad), ca, cb, va, vb)
+        check(ccall(sym(:lvb_gemm_ex), Cint,
+                    (Ref{GemmDesc}, Ref{Epilogue}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}, Ptr{Cvoid}),
+                    d, e, pa, pb, pc, stream))
+    end
     return C
 end
 

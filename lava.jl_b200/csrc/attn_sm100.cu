@@ -42,6 +42,7 @@ constexpr int kChunk = 128 * 128;       // bytes of one 128-row x 64-element swi
 struct AttnParams {
   int B, Hq, Hkv, Sq, Skv, group, num_pairs, causal;
   int total_items;             // num_pairs · B · Hq work items
+  int tail_heads;              // the last heads' items are handed out heaviest first
   int* work_counter;           // zero at launch; items are taken from it in order
   float scale_log2;
   void* O;
@@ -80,15 +81,26 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 
 // Geometry of one work item = (batch·head, pair of 128-row query tiles). Items are numbered
 // head by head, the heaviest causal pair of a head first, and handed out in that order, so
-// the CTAs running at any moment work on a few heads and share their K/V blocks in L2.
+// the CTAs running at any moment work on a few heads and share their K/V blocks in L2. The
+// items of the last `tail_heads` heads (about two waves of items) are numbered heaviest pair
+// first across those heads instead: the last items taken are then the lightest, and the CTAs
+// finish together (longest-first), while those heads' K/V still fit in L2.
 struct AttnItem {
   int b, h, hk, q0, n_tile0, n_tile1, n_blocks;
 };
 
 __device__ __forceinline__ AttnItem attn_item(int item, const AttnParams& p) {
   AttnItem it;
-  const int bh = item / p.num_pairs;
-  const int pair = p.num_pairs - 1 - (item - bh * p.num_pairs);
+  const int tail_start = p.total_items - p.tail_heads * p.num_pairs;
+  int bh, pair;
+  if (item >= tail_start) {
+    const int j = item - tail_start;
+    bh = p.B * p.Hq - p.tail_heads + j % p.tail_heads;
+    pair = p.num_pairs - 1 - j / p.tail_heads;
+  } else {
+    bh = item / p.num_pairs;
+    pair = p.num_pairs - 1 - (item - bh * p.num_pairs);
+  }
   it.b = bh / p.Hq;
   it.h = bh - it.b * p.Hq;
   it.hk = it.h / p.group;
@@ -633,6 +645,13 @@ int attn_launch(const lvb_attn_desc* d, const void* Q, const void* K, const void
     return fail(LVB_ERR_UNSUPPORTED, op, "more than 2^31 query-tile pairs", "split the batch");
   p.total_items = (int)items;
   const int ctas = (int)std::min<long long>(items, std::max(1, dev->sm_count));
+  // Causal items differ in length: the last ~two waves of items (whole heads) go
+  // longest-first (equal-length items gain nothing from it).
+  p.tail_heads = 0;
+  if (p.causal) {
+    const long long want = (2LL * ctas + p.num_pairs - 1) / p.num_pairs;
+    p.tail_heads = (int)std::min<long long>(B * Hq, std::max<long long>(1, want));
+  }
   // The item counter: zeroed on the stream before the launch, freed after it.
   void* ws = nullptr;
   cudaError_t e = workspace_alloc(dev, &ws, 16, stream);
