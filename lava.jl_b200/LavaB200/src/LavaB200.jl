@@ -34,7 +34,7 @@ using LinearAlgebra: Transpose, transpose
 import KernelInterface as KI
 
 export B200Backend, B200Array, gemm!, attention!, device_status, caps_raw, matrix_shapes_raw,
-       pe_program, PeProgram,
+       pe_program, PeProgram, pe_ifelse, pe_eq, pe_rsqrt, pe_erf,
        LavaB200Error, BFloat16, shard_range, comm_unique_id, Comm, allgather!
 
 const libpath = Ref{String}("")

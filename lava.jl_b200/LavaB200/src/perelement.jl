@@ -127,20 +127,22 @@ function Base.fma(a::PeVal, b::Union{PeVal,Real}, c::Union{PeVal,Real})
     x, y, z = (pe_f(tr, pe_lift(tr, v, :f)) for v in (a, b, c))
     return pe_node!(tr, :FFMA, [x.id, y.id, z.id], UInt32(0), :f)
 end
-function Base.ifelse(c::PeVal, a, b)
-    c.kind === :i || throw(ArgumentError("pe_program: ifelse needs a comparison as its condition"))
+# `ifelse` is a builtin (no methods can be added), so the traced select has its own name.
+"""`pe_ifelse(c, a, b)`: `c ? a : b` element-wise, `c` a comparison of traced values."""
+function pe_ifelse(c::PeVal, a, b)
+    c.kind === :i || throw(ArgumentError("pe_program: pe_ifelse needs a comparison as its condition"))
     tr = c.tr
     x, y, kind = pe_unify(tr, a, b)
     return pe_node!(tr, :SELECT, [c.id, x.id, y.id], UInt32(0), kind)
 end
-Base.Bool(::PeVal) = throw(ArgumentError("pe_program: a traced value has no truth value; use ifelse"))
+Base.Bool(::PeVal) = throw(ArgumentError("pe_program: a traced value has no truth value; use pe_ifelse"))  # Bool(v); `if v` is a TypeError
 
 """
     pe_program(f) -> PeProgram
 
 Trace `f(x, row, col, e)` — `x`, `e` Float32, `row`, `col` 0-based Int32 — into the library's
 per-element program. Supported: `+ - * /`, unary `-`, `abs`, `< <= > >=`, `pe_eq`, `min`,
-`max`, `exp`, `exp2`, `log`, `tanh`, `sqrt`, `floor`, `fma`, `ifelse`, `pe_rsqrt`, `pe_erf`.
+`max`, `exp`, `exp2`, `log`, `tanh`, `sqrt`, `floor`, `fma`, `pe_ifelse`, `pe_rsqrt`, `pe_erf`.
 At most 32 instructions and 8 values alive at once.
 """
 function pe_program(f)

@@ -49,6 +49,18 @@ using LinearAlgebra
         @info "Lava not installed: backend-form query tests not run"
     end
 
+    @testset "per-element programs are traced (no GPU)" begin
+        p = pe_program((x, r, c, e) -> x * 2.0f0 + c)
+        ops = [p.code[i].op for i in 1:p.n]
+        @test LavaB200.PE_OPS[:FMUL] in ops && LavaB200.PE_OPS[:I2F] in ops &&
+              LavaB200.PE_OPS[:FADD] in ops && p.n <= 32
+        q = pe_program((x, r, c, e) -> pe_ifelse(c > r, -Inf32, 0.125f0 * x))
+        @test LavaB200.PE_OPS[:SELECT] in [q.code[i].op for i in 1:q.n]
+        st = ccall(LavaB200.sym(:lvb_pe_program_check), Cint, (Ref{PeProgram},), q)
+        @test st == 0
+        @test_throws TypeError pe_program((x, r, c, e) -> x > 0 ? x : -x)   # non-Bool condition
+    end
+
     @testset "shards and communicator ids (no GPU)" begin
         @test [shard_range(1000, 2, r; align = 128) for r in 0:1] == [(0, 512), (512, 488)]
         id = comm_unique_id()
@@ -80,6 +92,28 @@ using LinearAlgebra
                   residual = dC, activation = :relu)
             ref = max.(Float64.(A) * Float64.(B) .+ Float64.(bias) .+ Float64.(R), 0.0)
             @test maximum(abs.(Array(dC) .- ref)) <= 1e-2
+            @test device_status() == (0, 0, 0)
+        end
+        @testset "gemm! coopmat_mul, per-element function, clamps (GPU)" begin
+            M, N, K = 200, 136, 100
+            A = Float16.(rand(Float32, M, K) .* 2 .- 1)
+            B = Float16.(rand(Float32, K, N) .* 2 .- 1)
+            S = rand(Float32, M, N) .* 2 .- 1
+            E = rand(Float32, M, N) .- 0.5f0
+            dC = B200Array{Float32}(undef, M, N)
+            gemm!(dC, B200Array(A), B200Array(B); mul = B200Array(S), extra = B200Array(E),
+                  perelement = (x, r, c, e) -> pe_ifelse(c > r, -Inf32, 0.5f0 * x + e))
+            P = (Float64.(A) * Float64.(B)) .* S
+            ref = [j - 1 > i - 1 ? -Inf : 0.5 * P[i, j] + E[i, j] for i in 1:M, j in 1:N]
+            got = Array(dC)
+            @test all(isinf.(got) .== isinf.(ref))
+            fin = .!isinf.(ref)
+            @test maximum(abs.(got[fin] .- ref[fin])) <= 1e-2
+            # TO_EDGE on A and the constant 0.5 on B over k_pad = 128
+            gemm!(dC, B200Array(A), B200Array(B); k_pad = 128, a_clamp = :edge, b_clamp = 0.5)
+            Ap = hcat(Float64.(A), repeat(Float64.(A[:, end]), 1, 28))
+            Bp = vcat(Float64.(B), fill(0.5, 28, N))
+            @test maximum(abs.(Array(dC) .- Ap * Bp)) <= 1e-2
             @test device_status() == (0, 0, 0)
         end
         @testset "gemm! Int8 exact (GPU)" begin

@@ -889,9 +889,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       drain_acc<OUT, AB, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out, n_staged, [&] {
         tc_fence_before();
         __syncwarp();
-        // TMEM read (tcgen05.wait::ld) and fenced: a relaxed arrive suffices, and skips the
-        // cluster-scope release of the staging writes (small-K GEMM: +30 %).
-        if (lane == 0) bar_arrive_cluster_relaxed(mapa_shared(smem_u32(&tempty[acc]), 0));
+        // TMEM read (tcgen05.wait::ld) and fenced: a CTA-scope release suffices, and skips
+        // the cluster-scope release of the staging writes (small-K GEMM: +30 %).
+        if (lane == 0) bar_arrive_cluster_cta(mapa_shared(smem_u32(&tempty[acc]), 0));
       });
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;

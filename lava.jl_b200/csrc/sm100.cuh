@@ -431,14 +431,16 @@ __device__ __forceinline__ void bar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
-// The same arrive without release semantics, for a hand-off whose only hazard is tcgen05
-// state: TMEM columns this thread read with tcgen05.ld, completed by tcgen05.wait::ld and
-// ordered before the arrive by tcgen05.fence::before_thread_sync; the waiter reads no memory
-// this thread wrote. A release at cluster scope would first wait for all of the thread's
-// earlier memory operations (an epilogue's shared-memory staging and stores) to become
-// visible across the cluster: measured ~1,100 clk per tile in the GEMM epilogue.
-__device__ __forceinline__ void bar_arrive_cluster_relaxed(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+// The same arrive with release at CTA scope (the PTX default for mbarrier.arrive), for a
+// hand-off whose only hazard is tcgen05 state: TMEM columns this thread read with tcgen05.ld,
+// completed by tcgen05.wait::ld and ordered before the arrive by
+// tcgen05.fence::before_thread_sync; the waiter reads no memory this thread wrote. A release
+// at cluster scope would first wait for all of the thread's earlier memory operations (an
+// epilogue's shared-memory staging and stores) to become visible across the cluster:
+// measured ~1,100 clk per tile in the GEMM epilogue; the CTA-scope release costs nothing
+// measurable there (small-K GEMM within 0.1 % of a relaxed arrive).
+__device__ __forceinline__ void bar_arrive_cluster_cta(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 // 2-D tiled load into this CTA's shared memory whose completion bytes are signalled on an

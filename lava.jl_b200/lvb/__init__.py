@@ -331,6 +331,8 @@ def _layout2d(t, name: str):
         raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm: {name} must be 2-D")
     r, c = t.shape
     s0, s1 = t.stride()
+    if r == 0 or c == 0:            # an empty operand has no layout to read
+        return 1, max(c, 1)
     if s1 == 1 and (r <= 1 or s0 >= max(c, 1)):
         return 1, max(s0, c, 1)
     if s0 == 1 and (c <= 1 or s1 >= max(r, 1)):
@@ -365,13 +367,21 @@ def _stream_ptr(stream) -> Optional[int]:
 
 
 def _cmatrix(C_, t, what):
-    """(pointer, type, leading dimension) of an M×N epilogue operand in C's layout."""
+    """(pointer, type, leading dimension) of an M×N epilogue operand read in C's layout (a
+    single row or column reads the same in either, whatever strides torch gave it)."""
     if tuple(t.shape) != tuple(C_.shape):
         raise LavaError(LVB_ERR_INVALID_ARG, f"lvb_gemm_ex: {what} must have C's shape")
-    rm, ld = _layout2d(t, what)
     crm, _ = _layout2d(C_, "C")
-    if rm != crm and min(C_.shape) > 1:
-        raise LavaError(LVB_ERR_UNSUPPORTED, f"lvb_gemm_ex: {what} must have C's layout")
+    r, c = t.shape
+    s0, s1 = t.stride()
+    if crm:
+        if c > 1 and s1 != 1:
+            raise LavaError(LVB_ERR_UNSUPPORTED, f"lvb_gemm_ex: {what} must have C's layout")
+        ld = s0 if r > 1 else max(c, 1)
+    else:
+        if r > 1 and s0 != 1:
+            raise LavaError(LVB_ERR_UNSUPPORTED, f"lvb_gemm_ex: {what} must have C's layout")
+        ld = s1 if c > 1 else max(r, 1)
     return t.data_ptr(), dtype_of(t), ld
 
 
