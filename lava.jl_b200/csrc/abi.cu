@@ -550,33 +550,47 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   const int64_t kM = out->swap_ab ? d->N : d->M;
   const int64_t kN = out->swap_ab ? d->M : d->N;
   const int64_t tiles_m = (kM + 127) / 128;
+  // MN-contiguous operands (A column-major, B row-major) are read MN-major in place when they
+  // are 16-bit; 8-bit ones are copied K-major first.
+  const int es = dtype_size(d->a_type);
+  const bool a_mn = !d->a_rowmajor, b_mn = d->b_rowmajor != 0;
+  out->repack_a = (d->lda * es) % 16 != 0 || (a_mn && es == 1);
+  out->repack_b = (d->ldb * es) % 16 != 0 || (b_mn && es == 1);
+  out->a_mnmajor = a_mn && !out->repack_a;
+  out->b_mnmajor = b_mn && !out->repack_b;
+  const bool kb_mn = out->swap_ab ? out->a_mnmajor : out->b_mnmajor;
+  const bool out32 = dtype_size(d->c_type) == 4;
   // Pick the tile width by estimated efficiency: wave quantisation times the intrinsic
   // efficiency of the narrower MMA (operand re-reads grow as BN shrinks).
-  // Candidate 512 stands for the CTA-pair kernel (256x256 tiles, one tile per two SMs).
-  // LVB_GEMM_TILE=512|256|128|64 forces one (tuning).
-  const int cands[4] = {512, 256, 128, 64};
-  const double intrinsic[4] = {1.08, 1.0, 0.86, 0.62};
+  // Candidates 512 and 448 stand for the CTA-pair kernel with 256×256 / 256×224 tiles (one
+  // tile per two SMs; the 224-wide tile for 32-bit outputs with B read K-major: it makes
+  // whole waves of 8192-wide outputs at 1024, 2048 or 4096 rows).
+  // LVB_GEMM_TILE=512|448|256|128|64 forces one (tuning).
+  const int cands[5] = {512, 448, 256, 128, 64};
+  const double intrinsic[5] = {1.08, 1.0, 1.0, 0.86, 0.62};
   static const int forced = [] {
     const char* s = std::getenv("LVB_GEMM_TILE");
     return s ? std::atoi(s) : 0;
   }();
   double best = -1;
   int bn = 256;
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 5; ++i) {
     if (forced && cands[i] != forced) continue;
-    const bool pair = cands[i] == 512;
+    if (cands[i] == 448 && (!out32 || kb_mn)) continue;
+    const bool pair = cands[i] >= 448;
+    const int64_t pw = cands[i] / 2;          // the pair's tile width
     const int64_t tm = pair ? (kM + 255) / 256 : tiles_m;
-    const int64_t tn = pair ? (kN + 255) / 256 : (kN + cands[i] - 1) / cands[i];
+    const int64_t tn = pair ? (kN + pw - 1) / pw : (kN + cands[i] - 1) / cands[i];
     const int64_t slots = pair ? std::max(1, sm_count / 2) : sm_count;
     const int64_t tiles = tm * tn;
     const int64_t waves = (tiles + slots - 1) / slots;
     const double eff = waves ? intrinsic[i] * (double)tiles / (double)(waves * slots) : 0;
     if (eff > best + 1e-9) { best = eff; bn = cands[i]; }
   }
-  const bool pair = bn == 512;
+  const bool pair = bn >= 448;
   out->cta_pair = pair ? 1 : 0;
   out->tile_m = pair ? 256 : 128;
-  out->tile_n = pair ? 256 : bn;
+  out->tile_n = pair ? bn / 2 : bn;
   out->tile_k = 128 / dtype_size(d->a_type);
   out->stages = gemm_stages(bn);
   out->tiles = (int32_t)(((kM + out->tile_m - 1) / out->tile_m) *
@@ -588,14 +602,6 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   out->instr_m = out->tile_m;
   out->instr_n = out->tile_n;
   out->instr_k = (d->a_type == LVB_I8 || d->a_type == LVB_U8) ? 32 : 16;
-  // MN-contiguous operands (A column-major, B row-major) are read MN-major in place when they
-  // are 16-bit; 8-bit ones are copied K-major first.
-  const int es = dtype_size(d->a_type);
-  const bool a_mn = !d->a_rowmajor, b_mn = d->b_rowmajor != 0;
-  out->repack_a = (d->lda * es) % 16 != 0 || (a_mn && es == 1);
-  out->repack_b = (d->ldb * es) % 16 != 0 || (b_mn && es == 1);
-  out->a_mnmajor = a_mn && !out->repack_a;
-  out->b_mnmajor = b_mn && !out->repack_b;
   out->launches = d->K == 0 ? 1 : 1 + out->repack_a + out->repack_b;
   return LVB_OK;
 }

@@ -27,6 +27,7 @@
 //   * persistent grid (one CTA per SM), tiles visited in groups of GROUP_M row-tiles so the
 //     ~148 tiles in flight share A rows and B columns in L2.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -42,6 +43,7 @@ enum AbKind { AB_F16 = 0, AB_BF16 = 1, AB_S8 = 2, AB_U8 = 3 };
 enum OutKind { OUT_F32 = 0, OUT_F16 = 1, OUT_BF16 = 2, OUT_I32 = 3 };
 
 constexpr int kBM = 128;
+constexpr int kMaxDevices = 128;
 constexpr int kRowBytes = 128;                 // K bytes per stage row (64 f16 / 128 i8)
 constexpr int kAStageBytes = kBM * kRowBytes;  // 16 KB
 constexpr int kThreads = 256;
@@ -473,8 +475,8 @@ __device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap
                                           uint32_t t_row, int m, int m0w, int n_base,
                                           float bias_m, uint32_t s_out, uint32_t& n_staged,
                                           Release release) {
-  static_assert(NCH % 2 == 0, "chunks are drained in pairs");
   constexpr bool k16 = OUT == OUT_F16 || OUT == OUT_BF16;
+  static_assert(NCH % 2 == 0 || !k16, "16-bit outputs are stored in pairs of chunks");
   const bool m_ok = m < p.M;
   uint32_t ra[32], rb[32];
   auto handle = [&](uint32_t (&r)[32], int c) {
@@ -501,6 +503,13 @@ __device__ __forceinline__ void drain_acc(const GemmParams& p, const CUtensorMap
   tmem_wait_ld(ra);
 #pragma unroll 1
   for (int c = 0; c < NCH; c += 2) {
+    if constexpr (NCH % 2 == 1) {
+      if (c + 1 == NCH) {   // the odd last chunk: already in registers
+        release();
+        handle(ra, c);
+        break;
+      }
+    }
     tmem_ld32(t_row + (c + 1) * 32, rb);
     handle(ra, c);
     tmem_wait_ld(rb);
@@ -709,29 +718,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 // a third); the even CTA issues the MMAs, both CTAs' TMA loads complete on its barrier, and
 // its commits arrive on both CTAs' barriers. Each CTA's epilogue drains its own TMEM rows.
 // ----------------------------------------------------------------------------------------
+// The pair's tile is 256 × BNP: BNP = 256, or 224 for 32-bit outputs (8192 = 36.6 × 224: 37
+// column tiles, so 1024, 2048 or 4096 rows of an 8192-wide output make whole waves of 74
+// pairs). CTA r stages B rows [BNP/2·r, BNP/2·(r+1)) of the tile.
 constexpr int kPairStages = 6;
 constexpr int kPairHalfBytes = 128 * kRowBytes;             // 16 KB: 128 rows x 128 B
-constexpr int kPairStageBytes = 2 * kPairHalfBytes;         // A half + B half
+constexpr int kPairStageBytes = 2 * kPairHalfBytes;         // A half + B half (BNP = 256)
 constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + kStoreBytes + 256 + 1024;
 
-template <int AB, int OUT>
+template <int AB, int OUT, int BNP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ GemmParams p) {
+  static_assert(BNP == 256 || (BNP == 224 && (OUT == OUT_F32 || OUT == OUT_I32)),
+                "the 224-wide pair tile drains 7 chunks: 32-bit outputs only");
   constexpr int S = kPairStages;
+  constexpr int kBHalfRows = BNP / 2;
+  constexpr int kBHalfBytes = kBHalfRows * kRowBytes;       // 1 KB multiple: swizzle atoms
+  constexpr int kStageBytes = kPairHalfBytes + kBHalfBytes;
   constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
   constexpr int kElemsPerRow = kInt ? 128 : 64;
   constexpr int kMmaK = kInt ? 32 : 16;
   constexpr int kMmasPerStage = kElemsPerRow / kMmaK;
   constexpr uint32_t kDescStep = (kMmaK * (kInt ? 1 : 2)) >> 4;
   constexpr uint32_t kIdesc =
-      kInt ? make_idesc(2, AB == AB_S8 ? 1 : 0, AB == AB_S8 ? 1 : 0, 0, 0, 256, 256)
-           : make_idesc(1, AB == AB_BF16 ? 1 : 0, AB == AB_BF16 ? 1 : 0, 0, 0, 256, 256);
+      kInt ? make_idesc(2, AB == AB_S8 ? 1 : 0, AB == AB_S8 ? 1 : 0, 0, 0, 256, BNP)
+           : make_idesc(1, AB == AB_BF16 ? 1 : 0, AB == AB_BF16 ? 1 : 0, 0, 0, 256, BNP);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   uint8_t* sA = smem;                        // [S][128 rows][128 B]
-  uint8_t* sB = smem + S * kPairHalfBytes;   // [S][128 rows][128 B]
+  uint8_t* sB = smem + S * kPairHalfBytes;   // [S][BNP/2 rows][128 B]
   uint8_t* sStore = smem + S * kPairStageBytes;    // [4 epilogue warps][2][32×32 elements]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
   uint64_t* full = bars;            // [S]  leader: both CTAs' TMA bytes
@@ -792,11 +809,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar(&empty[stage], phase ^ 1, g, 31, t)) { ok = false; break; }
         const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
-        if (leader) bar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
+        if (leader) bar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
         uint8_t* a_dst = sA + stage * kPairHalfBytes;
-        uint8_t* b_dst = sB + stage * kPairHalfBytes;
+        uint8_t* b_dst = sB + stage * kBHalfBytes;
         const int a_row = tm * 256 + 128 * (int)rank;
-        const int b_row = tn * 256 + 128 * (int)rank;
+        const int b_row = tn * BNP + kBHalfRows * (int)rank;
         if (!p.a_mn) {
           tma_load_2d_pair(a_dst, &tmA, kb * kElemsPerRow, a_row, full_leader, pol_a);
         } else {
@@ -833,12 +850,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
       if (!wait_bar_warp(&tempty[acc], acc_phase ^ 1, g, 32, t)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * 256;
+      const uint32_t d_tmem = tmem_base + acc * BNP;
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!wait_bar_warp(&full[stage], phase, g, 33, t)) { ok = false; break; }
         tc_fence_after();
         const uint64_t adesc = stage_desc(a_base + stage * kPairHalfBytes, p.a_mn);
-        const uint64_t bdesc = stage_desc(b_base + stage * kPairHalfBytes, p.b_mn);
+        const uint64_t bdesc = stage_desc(b_base + stage * kBHalfBytes, p.b_mn);
 #pragma unroll
         for (int k = 0; k < kMmasPerStage; ++k) {
           const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
@@ -885,8 +902,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool m_ok = m < p.M;
       const float bias_m =
           (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
-      const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * 256;
-      drain_acc<OUT, AB, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out, n_staged, [&] {
+      const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + acc * BNP;
+      drain_acc<OUT, AB, BNP / 32>(p, &tmD, t_row, m, m0 + ew * 32, tn * BNP, bias_m, s_out,
+                                   n_staged, [&] {
         tc_fence_before();
         __syncwarp();
         // TMEM read (tcgen05.wait::ld) and fenced: a CTA-scope release suffices, and skips
@@ -939,11 +957,16 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td
              cudaStream_t stream, DeviceState* dev) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<AB, OUT, BN>;
-  // The attribute is per function and per device; setting it every call is cheap and
-  // keeps this thread-safe without a cache.
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+  // The attribute is per function and per device: set once per device (two threads setting
+  // it at once set the same value).
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const int dv = dev->device >= 0 && dev->device < kMaxDevices ? dev->device : 0;
+  cudaError_t e;
+  if (!attr_set[dv].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+    attr_set[dv].store(true, std::memory_order_release);
+  }
   kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, td, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "kernel launch");
@@ -952,14 +975,19 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td
 
 // Persistent pair kernel: one cluster of 2 per SM pair, capped by how many clusters of this
 // kernel can be resident at once (GPC boundaries can leave an SM without a partner).
-template <int AB, int OUT>
+template <int AB, int OUT, int BNP>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                 const GemmParams& p, int clusters,
                 cudaStream_t stream, DeviceState* dev) {
-  auto kern = gemm_tc2_kernel<AB, OUT>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
-  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+  auto kern = gemm_tc2_kernel<AB, OUT, BNP>;
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const int dva = dev->device >= 0 && dev->device < kMaxDevices ? dev->device : 0;
+  cudaError_t e;
+  if (!attr_set[dva].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes);
+    if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+    attr_set[dva].store(true, std::memory_order_release);
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -972,19 +1000,18 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   static std::mutex mu;
-  static int resident[128] = {0};
-  int dv = dev->device >= 0 && dev->device < 128 ? dev->device : 0;
+  static int resident[kMaxDevices] = {0};
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (resident[dv] == 0) {
+    if (resident[dva] == 0) {
       int n = 0;
       cfg.gridDim = dim3(2 * std::max(1, dev->sm_count / 2));
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
         n = std::max(1, dev->sm_count / 2);
       cudaGetLastError();
-      resident[dv] = n;
+      resident[dva] = n;
     }
-    clusters = std::min(clusters, resident[dv]);
+    clusters = std::min(clusters, resident[dva]);
   }
   cfg.gridDim = dim3(2 * std::max(1, clusters));
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
@@ -995,7 +1022,14 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 template <int AB, int OUT>
 int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
               const GemmParams& p, int ctas, cudaStream_t s, DeviceState* dev) {
-  if (bn == 512) return launch_pair<AB, OUT>(ta, tb, td, p, ctas / 2, s, dev);
+  if (bn == 512) return launch_pair<AB, OUT, 256>(ta, tb, td, p, ctas / 2, s, dev);
+  if (bn == 448) {   // CTA pairs with 256 x 224 tiles (32-bit outputs, B read K-major)
+    if constexpr (OUT == OUT_F32 || OUT == OUT_I32) {
+      if (p.b_mn) return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "224-wide pair tile with MN-major B");
+      return launch_pair<AB, OUT, 224>(ta, tb, td, p, ctas / 2, s, dev);
+    }
+    return fail(LVB_ERR_UNSUPPORTED, "lvb_gemm", "224-wide pair tile with a 16-bit output");
+  }
   switch (bn) {
     case 256: return launch_t<AB, OUT, 256>(ta, tb, td, p, ctas, s, dev);
     case 128: return launch_t<AB, OUT, 128>(ta, tb, td, p, ctas, s, dev);
@@ -1008,7 +1042,8 @@ int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
 
 int gemm_smem_bytes(int bn) {
   switch (bn) {
-    case 512: return kPairSmemBytes;
+    case 512:
+    case 448: return kPairSmemBytes;
     case 256: return GemmCfg<256>::kSmemBytes;
     case 128: return GemmCfg<128>::kSmemBytes;
     case 64: return GemmCfg<64>::kSmemBytes;
@@ -1017,7 +1052,8 @@ int gemm_smem_bytes(int bn) {
 }
 int gemm_stages(int bn) {
   switch (bn) {
-    case 512: return kPairStages;
+    case 512:
+    case 448: return kPairStages;
     case 256: return GemmCfg<256>::kStages;
     case 128: return GemmCfg<128>::kStages;
     case 64: return GemmCfg<64>::kStages;
@@ -1499,7 +1535,8 @@ static int encode_maps(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const 
   st = kb_mn ? make_tmap_2d(tb, kB, esize, (uint64_t)kN, (uint64_t)d->K, (uint64_t)ldkb, 64, 64,
                             "lvb_gemm")
              : make_tmap_2d(tb, kB, esize, (uint64_t)d->K, (uint64_t)kN, (uint64_t)ldkb, box_k,
-                            plan.cta_pair ? 128u : (uint32_t)plan.tile_n, "lvb_gemm");
+                            plan.cta_pair ? (uint32_t)plan.tile_n / 2 : (uint32_t)plan.tile_n,
+                            "lvb_gemm");
   if (st) return st;
   const int osize = dtype_size(d->c_type);
   std::memset(td, 0, sizeof *td);
@@ -1633,7 +1670,8 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
 
   const int ab = ab_kind_of(d->a_type);
   const int out = out_kind_of(d->c_type);
-  const int bn = plan.cta_pair ? 512 : plan.tile_n;   // 512: the CTA-pair kernel
+  // 512 / 448: the CTA-pair kernel with 256 / 224-wide tiles
+  const int bn = plan.cta_pair ? 2 * plan.tile_n : plan.tile_n;
   const int ctas = plan.ctas;
   if (ab == AB_F16) {
     if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, td, p, ctas, stream, dev);

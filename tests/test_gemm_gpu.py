@@ -333,3 +333,36 @@ def test_small_k_many_tiles_exact(lvb, torch_cuda, c_rowmajor):
     for r0 in range(0, M, 1024):     # float64 BLAS is exact: partial sums below 2^53
         ref = (A[r0:r0 + 1024].astype(np.float64) @ B64).astype(np.int64)
         assert np.array_equal(C[r0:r0 + 1024].astype(np.int64), ref), r0
+
+
+@pytest.mark.parametrize("M,N,K,ab,out", [(2048, 7000, 512, "Int8", "Int32"),
+                                          (1000, 5000, 300, "BFloat16", "Float32"),
+                                          (1024, 8192, 1024, "Float16", "Float32"),
+                                          (2048, 6000, 384, "UInt8", "UInt32")])
+def test_pair_tile_224(lvb, torch_cuda, M, N, K, ab, out):
+    """CTA pairs with 256×224 tiles (32-bit outputs; the planner takes them when the
+    224-wide columns fill the waves better): seven 32-column chunks per drained accumulator, a
+    ragged last column tile (7000 = 31·224 + 56), every element checked."""
+    t = {"Int8": lvb.I8, "UInt8": lvb.U8, "BFloat16": lvb.BF16, "Float16": lvb.F16}[ab]
+    o = {"Int32": lvb.I32, "UInt32": lvb.U32, "Float32": lvb.F32}[out]
+    plan = lvb.gemm_plan(M, N, K, t, o, c_rowmajor=True)
+    assert plan.cta_pair == 1 and plan.tile_n == 224, (plan.cta_pair, plan.tile_n)
+    A, Bt = gemm_inputs(M, N, K, ab, seed=M + N)
+    C = run(lvb, torch_cuda, A, Bt, ab, out, c_rowmajor=True)
+    check(C, A, Bt.T, out)
+
+
+@pytest.mark.slow
+def test_split_shard_int8_1024_rows_exact(lvb, torch_cuda):
+    """One rank's share of C3 row-sharded over 8 GPUs: 1024×8192×8192 int8, 148 tiles of
+    256×224 (exactly two waves of 74 CTA pairs), 96 sampled rows exactly and every row's
+    exact checksum."""
+    plan = lvb.gemm_plan(1024, 8192, 8192, lvb.I8, lvb.I32, c_rowmajor=True)
+    assert plan.tile_n == 224 and plan.tiles == 148
+    A, Bt = gemm_inputs(1024, 8192, 8192, "Int8", seed=22)
+    C = run(lvb, torch_cuda, A, Bt, "Int8", "Int32", c_rowmajor=True)
+    rows = np.random.default_rng(2).choice(1024, 96, replace=False)
+    ref = (A[rows].astype(np.float64) @ Bt.T.astype(np.float64)).astype(np.int64)
+    assert np.array_equal(C[rows].astype(np.int64), ref)
+    colsum = Bt.astype(np.int64).sum(axis=0)
+    assert np.array_equal(C.astype(np.int64).sum(axis=1), A.astype(np.int64) @ colsum)

@@ -249,3 +249,28 @@ def test_clamp_k0_constant_and_checks(lvb, torch_cuda):
     with pytest.raises(lvb.LavaError) as e:
         lvb.gemm(C8, A8, B8, k_pad=32, a_clamp=200, b_clamp=1)
     assert e.value.status == lvb.LVB_ERR_INVALID_ARG
+
+
+def test_vocab_epilogue_on_pair_tile_224(lvb, torch_cuda):
+    """The fused epilogue (bias, residual, mul, activation, program, clamp) on the 256×224
+    CTA-pair tile, whose accumulator drains in seven 32-column chunks."""
+    from lvb.perelement import program, where
+    torch = torch_cuda
+    M, N, K, k_pad = 1024, 8192, 200, 256
+    plan = lvb.gemm_plan(M, N, K, lvb.F16, lvb.F32, c_rowmajor=True)
+    assert plan.cta_pair == 1 and plan.tile_n == 224
+    A, Bt = gemm_inputs(M, N, K, "Float16", seed=224)
+    g = np.random.default_rng(224)
+    S = g.uniform(-1, 1, (M, N)).astype(np.float32)
+    R = g.uniform(-1, 1, (M, N)).astype(np.float16)
+    bias = g.uniform(-1, 1, N).astype(np.float32)
+    prog = program(lambda x, r, c, e: where(c > r + 4000, 0.0, x))
+    got = run(lvb, torch, A, Bt, "Float16", "Float32", True, bias=dev(torch, bias, "Float32"),
+              residual=dev(torch, R, "Float16"), mul=dev(torch, S, "Float32"), activation="silu",
+              program=prog, k_pad=k_pad, a_clamp="edge", b_clamp=0.5)
+    ref = gemm_vocab_ref(A, Bt.T, "Float32", "Float16", bias=bias, residual=R, mul=S, act="silu",
+                         program=prog.code, k_pad=k_pad, a_clamp=("edge", 0),
+                         b_clamp=("constant", 0.5))
+    Ap = clamp_pad(A, k_pad, 1, "edge", 0, "Float16").astype(np.float64)
+    Bp = clamp_pad(Bt.T, k_pad, 0, "constant", 0.5, "Float16").astype(np.float64)
+    compare(got, ref, Ap, Bp, np.abs(R) + np.abs(bias), "Float32", L=1.1)
