@@ -272,9 +272,15 @@ def cpu_baseline(w, budget_s: float = 12.0):
 def run_reference(args, w):
     # Every host core, whatever the launcher set: torchrun exports OMP_NUM_THREADS=1, which
     # would leave the host BLAS on one thread (and shrink the time-sized sample) at N > 1.
+    # The BLAS reads its thread count when numpy loads it, and threadpoolctl acts only on
+    # libraries already loaded: set both, in that order.
+    ncpu = str(os.cpu_count() or 1)
+    for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = ncpu
+    import numpy  # noqa: F401  (loads the BLAS with the thread count above)
     try:
         from threadpoolctl import threadpool_limits
-        limits = threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+        limits = threadpool_limits(limits=int(ncpu), user_api="blas")
     except Exception:  # noqa: BLE001
         limits = None
     step, units, sample = cpu_step_factory(w, target_s=1.0)
