@@ -133,7 +133,9 @@ typedef struct lvb_gemm_plan {
   int32_t repack_a, repack_b;        /* operand copied K-major into an aligned stream-ordered
                                         workspace first (leading dimension or base not 16-byte
                                         aligned, or an 8-bit operand stored MN-contiguous) */
-  int32_t cta_pair;                  /* 1: 256x256 tiles on CTA pairs (tcgen05 cta_group::2) */
+  int32_t cta_pair;                  /* 1: tiles on CTA pairs (tcgen05 cta_group::2): 256x256,
+                                        256x224 (32-bit outputs), or 512x256 (tile_m 512: two
+                                        256-row blocks sharing each B stage) */
   int32_t a_mnmajor, b_mnmajor;      /* operand read by the tensor core MN-major, in place (A
                                         column-major / B row-major, 16-bit types) */
   int32_t gemv;                      /* 1: N == 1 or M == 1 — a matrix-vector product, streamed

@@ -562,24 +562,28 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   const bool out32 = dtype_size(d->c_type) == 4;
   // Pick the tile width by estimated efficiency: wave quantisation times the intrinsic
   // efficiency of the narrower MMA (operand re-reads grow as BN shrinks).
-  // Candidates 512 and 448 stand for the CTA-pair kernel with 256×256 / 256×224 tiles (one
-  // tile per two SMs; the 224-wide tile for 32-bit outputs with B read K-major: it makes
-  // whole waves of 8192-wide outputs at 1024, 2048 or 4096 rows).
-  // LVB_GEMM_TILE=512|448|256|128|64 forces one (tuning).
-  const int cands[5] = {512, 448, 256, 128, 64};
-  const double intrinsic[5] = {1.08, 1.0, 1.0, 0.86, 0.62};
+  // Candidates 1024, 512 and 448 stand for the CTA-pair kernels with 512×256, 256×256 and
+  // 256×224 tiles (one tile per two SMs; the 512-row tile shares each B stage between two
+  // 256-row blocks, a quarter less operand traffic per FLOP; the 224-wide tile for 32-bit
+  // outputs with B read K-major makes whole waves of 8192-wide outputs at 1024 or 2048 rows).
+  // LVB_GEMM_TILE=1024|512|448|256|128|64 forces one (tuning).
+  const int cands[6] = {1024, 512, 448, 256, 128, 64};
+  // The tall pair tile's factor: C2 at 1,512 vs 1,425 TFLOP/s (20 launches) and 1,335 vs
+  // 1,279 (400 launches, at the power cap) against the square pair tile.
+  const double intrinsic[6] = {1.12, 1.08, 1.0, 1.0, 0.86, 0.62};
   static const int forced = [] {
     const char* s = std::getenv("LVB_GEMM_TILE");
     return s ? std::atoi(s) : 0;
   }();
   double best = -1;
   int bn = 256;
-  for (int i = 0; i < 5; ++i) {
+  for (int i = 0; i < 6; ++i) {
     if (forced && cands[i] != forced) continue;
     if (cands[i] == 448 && (!out32 || kb_mn)) continue;
     const bool pair = cands[i] >= 448;
-    const int64_t pw = cands[i] / 2;          // the pair's tile width
-    const int64_t tm = pair ? (kM + 255) / 256 : tiles_m;
+    const bool tall = cands[i] == 1024;        // 512 × 256 tiles on a CTA pair
+    const int64_t pw = tall ? 256 : cands[i] / 2;   // the pair's tile width
+    const int64_t tm = tall ? (kM + 511) / 512 : pair ? (kM + 255) / 256 : tiles_m;
     const int64_t tn = pair ? (kN + pw - 1) / pw : (kN + cands[i] - 1) / cands[i];
     const int64_t slots = pair ? std::max(1, sm_count / 2) : sm_count;
     const int64_t tiles = tm * tn;
@@ -589,8 +593,8 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
   }
   const bool pair = bn >= 448;
   out->cta_pair = pair ? 1 : 0;
-  out->tile_m = pair ? 256 : 128;
-  out->tile_n = pair ? bn / 2 : bn;
+  out->tile_m = bn == 1024 ? 512 : pair ? 256 : 128;
+  out->tile_n = bn == 1024 ? 256 : pair ? bn / 2 : bn;
   out->tile_k = 128 / dtype_size(d->a_type);
   out->stages = gemm_stages(bn);
   out->tiles = (int32_t)(((kM + out->tile_m - 1) / out->tile_m) *
@@ -599,7 +603,7 @@ int gemm_plan_c(const lvb_gemm_desc* d, int32_t sm_count, bool c_tma_ok, lvb_gem
                    : std::max(1, std::min<int32_t>(out->tiles, sm_count));
   out->smem_bytes = gemm_smem_bytes(bn);
   out->tmem_cols = pair ? 512 : 2 * bn;
-  out->instr_m = out->tile_m;
+  out->instr_m = pair ? 256 : out->tile_m;
   out->instr_n = out->tile_n;
   out->instr_k = (d->a_type == LVB_I8 || d->a_type == LVB_U8) ? 32 : 16;
   out->launches = d->K == 0 ? 1 : 1 + out->repack_a + out->repack_b;

@@ -927,6 +927,244 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ----------------------------------------------------------------------------------------
+// Tall CTA-pair variant: the pair computes a 512 × 256 tile as two 256-row blocks, each one
+// cta_group::2 MMA chain (M = 256, N = 256) into its own TMEM accumulator (columns 0-255 and
+// 256-511 of both CTAs): per 64-deep k-block a CTA stages two 128-row halves of A (one per
+// row block) and one 128-row half of B, so each B half feeds twice the MMAs of the square
+// pair kernel and the operand traffic from L2 per FLOP is 3/4 of it (48 KB per CTA for two
+// 256×256×64 products instead of 32 KB for one). TMEM then holds one tile, not two: the
+// epilogue drains block 0, then block 1, and the MMA warp starts the next tile's block-0
+// products as soon as block 0 is drained, running up to the ring's depth ahead of block 1
+// (whose products wait for block 1's drain) and catching block 1 up once it is free.
+// ----------------------------------------------------------------------------------------
+constexpr int kTallStages = 4;
+constexpr int kTallStageBytes = 3 * kPairHalfBytes;         // A half 0, A half 1, B half
+constexpr int kTallSmemBytes = kTallStages * kTallStageBytes + kStoreBytes + 256 + 1024;
+static_assert(kTallSmemBytes <= 232448, "tall pair stages exceed the shared-memory budget");
+
+template <int AB, int OUT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tall_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ GemmParams p) {
+  constexpr int S = kTallStages;
+  constexpr bool kInt = (AB == AB_S8 || AB == AB_U8);
+  constexpr int kElemsPerRow = kInt ? 128 : 64;
+  constexpr int kMmaK = kInt ? 32 : 16;
+  constexpr int kMmasPerStage = kElemsPerRow / kMmaK;
+  constexpr uint32_t kDescStep = (kMmaK * (kInt ? 1 : 2)) >> 4;
+  constexpr uint32_t kIdesc =
+      kInt ? make_idesc(2, AB == AB_S8 ? 1 : 0, AB == AB_S8 ? 1 : 0, 0, 0, 256, 256)
+           : make_idesc(1, AB == AB_BF16 ? 1 : 0, AB == AB_BF16 ? 1 : 0, 0, 0, 256, 256);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  uint8_t* sA = smem;                              // [S][2 halves][128 rows][128 B]
+  uint8_t* sB = smem + S * 2 * kPairHalfBytes;     // [S][128 rows][128 B]
+  uint8_t* sStore = smem + S * kTallStageBytes;    // [4 epilogue warps][2][32×32 elements]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStore + kStoreBytes);
+  uint64_t* full = bars;            // [S]  leader: both CTAs' TMA bytes
+  uint64_t* empty = bars + S;       // [S]  both: both row blocks' MMAs done with the stage
+  uint64_t* tfull = bars + 2 * S;   // [2]  both: row block b's accumulator ready
+  uint64_t* tempty = tfull + 2;     // [2]  leader: 8 epilogue warps drained row block b
+  uint64_t* drain = tempty + 2;     // [1]  leader
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      bar_init(&tfull[b], 1);
+      bar_init(&tempty[b], 8);
+    }
+    bar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();        // barrier.cluster is .aligned: whole warps
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t filled_mask = 0;
+    uint32_t last_phase[kTallStages] = {0};
+    bool ok = true;
+    const uint64_t pol_a = p.l2_mode == 2 ? policy_evict_normal() : policy_for(p.l2_mode, true);
+    const uint64_t pol_b = p.l2_mode == 2 ? policy_evict_normal() : policy_for(p.l2_mode, false);
+    for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!wait_bar(&empty[stage], phase ^ 1, g, 41, t)) { ok = false; break; }
+        const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+        if (leader) bar_arrive_expect_tx(&full[stage], 2 * kTallStageBytes);
+        uint8_t* b_dst = sB + stage * kPairHalfBytes;
+        const int b_row = tn * 256 + 128 * (int)rank;
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* a_dst = sA + (stage * 2 + h) * kPairHalfBytes;
+          const int a_row = tm * 512 + 256 * h + 128 * (int)rank;
+          if (!p.a_mn) {
+            tma_load_2d_pair(a_dst, &tmA, kb * kElemsPerRow, a_row, full_leader, pol_a);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, a_row, kb * 64, full_leader, pol_a);
+            tma_load_2d_pair(a_dst + kMnChunkBytes, &tmA, a_row + 64, kb * 64, full_leader, pol_a);
+          }
+        }
+        if (!p.b_mn) {
+          tma_load_2d_pair(b_dst, &tmB, kb * kElemsPerRow, b_row, full_leader, pol_b);
+        } else {
+          tma_load_2d_pair(b_dst, &tmB, b_row, kb * 64, full_leader, pol_b);
+          tma_load_2d_pair(b_dst + kMnChunkBytes, &tmB, b_row + 64, kb * 64, full_leader, pol_b);
+        }
+        filled_mask |= 1u << stage;
+        last_phase[stage] = phase;
+        if (++stage == S) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok && leader) {
+      for (int s = 0; s < S; ++s)
+        if (filled_mask & (1u << s)) drain_wait(&full[s], last_phase[s], p.timeout_ns);
+    }
+  } else if (warp == 1 && leader) {
+    // ---------------- MMA issuer (even CTA of the pair; one elected lane issues) --------
+    // Two cursors walk the same ring: row block 0 (s0) leads, row block 1 (s1) follows and
+    // releases each stage to the producer once both blocks have consumed it.
+    int s0 = 0, s1 = 0;
+    uint32_t ph0 = 0, ph1 = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    const uint32_t a_base = smem_u32(sA);
+    const uint32_t b_base = smem_u32(sB);
+    const uint32_t idesc = kIdesc | ((uint32_t)p.a_mn << 15) | ((uint32_t)p.b_mn << 16);
+    const uint32_t a_step = p.a_mn ? (16 * 128) >> 4 : kDescStep;
+    const uint32_t b_step = p.b_mn ? (16 * 128) >> 4 : kDescStep;
+    auto issue = [&](int blk, int stage, bool first) {
+      const uint64_t adesc = stage_desc(a_base + (stage * 2 + blk) * kPairHalfBytes, p.a_mn);
+      const uint64_t bdesc = stage_desc(b_base + stage * kPairHalfBytes, p.b_mn);
+      const uint32_t d_tmem = tmem_base + 256 * blk;
+#pragma unroll
+      for (int k = 0; k < kMmasPerStage; ++k) {
+        const uint32_t accum = (!first || k > 0) ? 1u : 0u;
+        if (elect_one()) {
+          if constexpr (kInt)
+            mma_i8_ss_pair(d_tmem, adesc + k * kDescStep, bdesc + k * kDescStep, kIdesc, accum);
+          else
+            mma_f16_ss_pair(d_tmem, adesc + k * a_step, bdesc + k * b_step, idesc, accum);
+        }
+      }
+    };
+    auto commit_both = [&](uint64_t* bar) {
+      const uint32_t a = smem_u32(bar);
+      if (elect_one()) {
+        mma_commit_pair(mapa_shared(a, 0));
+        mma_commit_pair(mapa_shared(a, 1));
+      }
+    };
+    for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
+      if (!wait_bar_warp(&tempty[0], acc_phase ^ 1, g, 42, t)) { ok = false; break; }
+      tc_fence_after();
+      bool free1 = false;
+      int kb1 = 0;
+      // row block 1's products for k-blocks kb1..upto (their stages are full already)
+      auto catch_up = [&](int upto) {
+        for (; kb1 <= upto; ++kb1) {
+          issue(1, s1, kb1 == 0);
+          commit_both(&empty[s1]);
+          if (++s1 == S) { s1 = 0; ph1 ^= 1; }
+        }
+      };
+      for (int kb0 = 0; kb0 < p.num_kb; ++kb0) {
+        if (!wait_bar_warp(&full[s0], ph0, g, 43, t)) { ok = false; break; }
+        tc_fence_after();
+        issue(0, s0, kb0 == 0);
+        if (++s0 == S) { s0 = 0; ph0 ^= 1; }
+        if (!free1) {
+          free1 = __all_sync(0xffffffffu, bar_test_wait(smem_u32(&tempty[1]), acc_phase ^ 1));
+          if (!free1 && kb0 + 1 - kb1 >= S) {   // every stage is held: block 1 must move
+            if (!wait_bar_warp(&tempty[1], acc_phase ^ 1, g, 44, t)) { ok = false; break; }
+            free1 = true;
+          }
+          if (free1) tc_fence_after();
+        }
+        if (free1) catch_up(kb0);
+      }
+      if (!ok) break;
+      commit_both(&tfull[0]);
+      if (!free1) {
+        if (!wait_bar_warp(&tempty[1], acc_phase ^ 1, g, 44, t)) { ok = false; break; }
+        tc_fence_after();
+      }
+      catch_up(p.num_kb - 1);
+      commit_both(&tfull[1]);
+      acc_phase ^= 1;
+    }
+    if (elect_one()) mma_commit_pair(mapa_shared(smem_u32(drain), 0));
+    drain_wait(drain, 0, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ---------------- epilogue (both CTAs, own TMEM rows; block 0, then block 1) -------
+    const int ew = warp - 4;
+    const int row = ew * 32 + lane;
+    const uint32_t s_out = smem_u32(sStore) + ew * 2 * kStoreBufBytes;
+    uint32_t n_staged = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int t = cluster_id; t < p.total_tiles && ok; t += nclusters) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      for (int blk = 0; blk < 2; ++blk) {
+        if (!wait_bar(&tfull[blk], acc_phase, g, 45, t)) { ok = false; break; }
+        tc_fence_after();
+        const int m0 = tm * 512 + 256 * blk + 128 * (int)rank;
+        const int m = m0 + row;
+        const bool m_ok = m < p.M;
+        const float bias_m =
+            (p.bias && p.bias_on_m && m_ok) ? load_as_f32(p.bias, p.bias_kind, m) : 0.f;
+        const uint32_t t_row = tmem_base + ((uint32_t)(ew * 32) << 16) + 256 * blk;
+        drain_acc<OUT, AB, 8>(p, &tmD, t_row, m, m0 + ew * 32, tn * 256, bias_m, s_out,
+                              n_staged, [&] {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) bar_arrive_cluster_cta(mapa_shared(smem_u32(&tempty[blk]), 0));
+        });
+      }
+      acc_phase ^= 1;
+    }
+    if (p.stage_out && lane == 0) bulk_wait_group<0>();  // stores done before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // the pair's MMAs are done with both CTAs' shared memory and TMEM
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------------------
 namespace {
@@ -1019,9 +1257,54 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return LVB_OK;
 }
 
+// The tall pair kernel (512 × 256 tiles), launched like launch_pair.
+template <int AB, int OUT>
+int launch_tall(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                const GemmParams& p, int clusters, cudaStream_t stream, DeviceState* dev) {
+  auto kern = gemm_tall_kernel<AB, OUT>;
+  static std::atomic<bool> attr_set[kMaxDevices];
+  const int dva = dev->device >= 0 && dev->device < kMaxDevices ? dev->device : 0;
+  cudaError_t e;
+  if (!attr_set[dva].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTallSmemBytes);
+    if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
+    attr_set[dva].store(true, std::memory_order_release);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kTallSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static std::mutex mu;
+  static int resident[kMaxDevices] = {0};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (resident[dva] == 0) {
+      int n = 0;
+      cfg.gridDim = dim3(2 * std::max(1, dev->sm_count / 2));
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0)
+        n = std::max(1, dev->sm_count / 2);
+      cudaGetLastError();
+      resident[dva] = n;
+    }
+    clusters = std::min(clusters, resident[dva]);
+  }
+  cfg.gridDim = dim3(2 * std::max(1, clusters));
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
+  if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cluster kernel launch");
+  return LVB_OK;
+}
+
 template <int AB, int OUT>
 int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
               const GemmParams& p, int ctas, cudaStream_t s, DeviceState* dev) {
+  if (bn == 1024) return launch_tall<AB, OUT>(ta, tb, td, p, ctas / 2, s, dev);
   if (bn == 512) return launch_pair<AB, OUT, 256>(ta, tb, td, p, ctas / 2, s, dev);
   if (bn == 448) {   // CTA pairs with 256 x 224 tiles (32-bit outputs, B read K-major)
     if constexpr (OUT == OUT_F32 || OUT == OUT_I32) {
@@ -1042,6 +1325,7 @@ int launch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const CUtens
 
 int gemm_smem_bytes(int bn) {
   switch (bn) {
+    case 1024: return kTallSmemBytes;
     case 512:
     case 448: return kPairSmemBytes;
     case 256: return GemmCfg<256>::kSmemBytes;
@@ -1052,6 +1336,7 @@ int gemm_smem_bytes(int bn) {
 }
 int gemm_stages(int bn) {
   switch (bn) {
+    case 1024: return kTallStages;
     case 512:
     case 448: return kPairStages;
     case 256: return GemmCfg<256>::kStages;
@@ -1670,8 +1955,9 @@ int gemm_launch_aligned(const lvb_gemm_desc* d, const lvb_gemm_plan& plan, const
 
   const int ab = ab_kind_of(d->a_type);
   const int out = out_kind_of(d->c_type);
-  // 512 / 448: the CTA-pair kernel with 256 / 224-wide tiles
-  const int bn = plan.cta_pair ? 2 * plan.tile_n : plan.tile_n;
+  // 1024: the tall CTA-pair kernel (512 × 256 tiles); 512 / 448: the CTA-pair kernel with
+  // 256 × 256 / 256 × 224 tiles
+  const int bn = plan.cta_pair ? (plan.tile_m == 512 ? 1024 : 2 * plan.tile_n) : plan.tile_n;
   const int ctas = plan.ctas;
   if (ab == AB_F16) {
     if (out == OUT_F32) return launch_bn<AB_F16, OUT_F32>(bn, ta, tb, td, p, ctas, stream, dev);

@@ -90,6 +90,19 @@ __device__ __forceinline__ bool bar_try_wait(uint32_t bar_addr, uint32_t parity)
   return ok != 0;
 }
 
+// Non-blocking test of the phase of parity `parity` (no suspension).
+__device__ __forceinline__ bool bar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase of parity `parity` to complete. Returns false (and raises
 // the abort flag) when the CTA was already aborting or the wall-clock limit expired.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const WaitGuard& g,

@@ -366,3 +366,20 @@ def test_split_shard_int8_1024_rows_exact(lvb, torch_cuda):
     assert np.array_equal(C[rows].astype(np.int64), ref)
     colsum = Bt.astype(np.int64).sum(axis=0)
     assert np.array_equal(C.astype(np.int64).sum(axis=1), A.astype(np.int64) @ colsum)
+
+
+@pytest.mark.parametrize("M,N,K,ab,out,c_rowmajor", [(4000, 4000, 256, "Float16", "Float16", True),
+                                                     (3000, 5000, 1000, "BFloat16", "BFloat16", False),
+                                                     (4000, 4000, 256, "Float16", "BFloat16", True)])
+def test_tall_pair_tile(lvb, torch_cuda, M, N, K, ab, out, c_rowmajor):
+    """CTA pairs with 512×256 tiles (two 256-row blocks sharing each B stage, one TMEM
+    accumulator each, the next tile's first block started while the second drains): ragged
+    rows (4000 = 7·512 + 416) and columns, both orientations of the product, every element
+    checked."""
+    t = {"BFloat16": lvb.BF16, "Float16": lvb.F16}[ab]
+    o = {"Float16": lvb.F16, "BFloat16": lvb.BF16}[out]
+    plan = lvb.gemm_plan(M, N, K, t, o, c_rowmajor=c_rowmajor)
+    assert plan.cta_pair == 1 and plan.tile_m == 512, (plan.tile_m, plan.tile_n)
+    A, Bt = gemm_inputs(M, N, K, ab, seed=M + K)
+    C = run(lvb, torch_cuda, A, Bt, ab, out, c_rowmajor=c_rowmajor)
+    check(C, A, Bt.T, out)
