@@ -142,13 +142,17 @@ def test_gemm_without_device_fails_loudly(lvb):
 
 def test_plans(lvb):
     p = lvb.gemm_plan(8192, 8192, 8192, lvb.F16, lvb.F16)
-    # large problems: 256x256 tiles on CTA pairs (cta_group::2), 74 pairs on 148 SMs
+    # large problems: 512x256 tiles on CTA pairs (cta_group::2: two 256x256 MMA chains, one
+    # per 256-row block), 74 pairs on 148 SMs
     assert p.cta_pair == 1
-    assert (p.tile_m, p.tile_n, p.tile_k, p.instr_m, p.instr_k) == (256, 256, 64, 256, 16)
+    assert (p.tile_m, p.tile_n, p.tile_k, p.instr_m, p.instr_k) == (512, 256, 64, 256, 16)
     # column-major C that can take TMA stores: computed as Cᵀ = BᵀAᵀ so the kernel's
     # n is C's contiguous dimension (each thread's columns are one contiguous run)
-    assert p.tiles == 32 * 32 and p.ctas == 148 and p.swap_ab == 1
-    assert p.tmem_cols == 512 and p.smem_bytes <= 232448 and p.stages == 6
+    assert p.tiles == 16 * 32 and p.ctas == 148 and p.swap_ab == 1
+    assert p.tmem_cols == 512 and p.smem_bytes <= 232448 and p.stages == 4
+    # fewer row blocks than pairs can fill in whole waves: 256x256 tiles on the pairs
+    sq = lvb.gemm_plan(4096, 8192, 8192, lvb.F16, lvb.F16, c_rowmajor=True)
+    assert (sq.tile_m, sq.tile_n, sq.stages) == (256, 256, 6)
     q = lvb.gemm_plan(8192, 8192, 8192, lvb.I8, lvb.I32)
     assert q.tile_k == 128 and q.instr_k == 32
     # a problem with fewer 256x256 tiles than SM pairs uses 1-CTA tiles
