@@ -52,6 +52,9 @@ WORKLOADS = {
                          seed=0, dtype="f16"),
     "gemm_i8": dict(kind="gemm", cfg="C3", M=8192, N=8192, K=8192, ab="Int8", out="Int32",
                     seed=2, dtype="int8"),
+    # one rank's share of C3 row-sharded over 8 GPUs (the `split` key's per-GPU problem at N=8)
+    "gemm_i8_shard8": dict(kind="gemm", cfg="C3-shard-of-8", M=1024, N=8192, K=8192,
+                           ab="Int8", out="Int32", seed=2, dtype="int8"),
     "gemm_bf16": dict(kind="gemm", cfg="C5-gemm", M=65536, N=8192, K=8192, ab="BFloat16",
                       out="BFloat16", seed=5, dtype="bf16"),
     # C2 with the fused epilogue C = gelu(A·B + bias + R) (bias per column, R fp16 M×N)
@@ -801,14 +804,14 @@ def run_gpu(args, w):
     # call), through the prepared call (the timed step), and replayed from a CUDA graph of
     # captured calls (about the kernel's own time)
     per_call = None
-    if w["kind"] == "gemm" and w["M"] * w["N"] * w["K"] <= 1 << 30 and not args.no_extras:
+    if w["kind"] == "gemm" and w["M"] * w["N"] * w["K"] <= 1 << 30 and args.extras == "all":
         per_call = host_path_breakdown(torch, step, stream)
 
     cublas = None
     if not args.no_extras:
         cublas = cublas_sanity(torch, w, ins, args.steps, args.warmup, stream)
     extras = None
-    if not args.no_extras and args.workload == "gemm_f16":
+    if args.extras == "all" and args.workload == "gemm_f16":
         torch.cuda.empty_cache()
         extras = measure_extras(args, torch, lvb, world, rank, local, stream, barrier,
                                 max_over_ranks)
@@ -905,14 +908,21 @@ def main():
                     help="skip the end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the attention / split-GEMM / cuBLAS keys of the default line")
+    ap.add_argument("--extras", default="all", choices=["all", "none", "cublas"],
+                    help="which of those keys to measure (cublas: only the cuBLAS figure; "
+                         "--no-extras is 'none')")
     args = ap.parse_args()
+    if args.no_extras:
+        args.extras = "none"
+    args.no_extras = args.extras == "none"
     w = WORKLOADS[args.workload]
     if args.steps is None:
         # about 2 s of timed device work at the expected rate
         args.steps = {"gemm_f16": 2000, "gemm_f16_512": 2000, "gemm_i8": 3000,
                       "gemm_bf16": 250, "attn_f16": 2000, "attn_bf16": 40,
                       "gemm_f16_fused": 2000, "gemm_f16_mn": 2000,
-                      "attn_decode_bf16": 10000, "gemv_i8": 20000}[args.workload]
+                      "attn_decode_bf16": 10000, "gemv_i8": 20000,
+                      "gemm_i8_shard8": 20000}[args.workload]
         if args.impl == "reference":
             args.steps = 5
     args.warmup = max(args.warmup, 3)
