@@ -548,7 +548,9 @@ def measure_extras(args, torch, lvb, world, rank, local, stream, sync, max_over_
             "parallelism": (f"(batch, kv-head) units sharded over {world} ranks, one problem"
                             if world > 1 else "single GPU"),
             "scaling": "strong" if world > 1 else None,
-            "roofline": tensor_roofline(fl, ms_l, steps, peaks, src),
+            "roofline": dict(tensor_roofline(fl, ms_l, steps, peaks, src),
+                             traffic=profile_traffic("attn_f16" if name == "C4" else "attn_bf16")
+                             if world == 1 else None),
             "clocks": clocks, "gpu_launches": steps * launches}
         del keep
         torch.cuda.empty_cache()
