@@ -9,22 +9,27 @@
 // then O / l stored through a clamped layout.
 //
 // How, per CTA = two 128-row query tiles of one (batch, query head):
-//   * TMEM: S_0 | S_1 | O_0 | O_1 = 512 columns. P_t (16-bit) overwrites the first 64
-//     columns of S_t once the softmax has read S_t into registers, and the P·V product
-//     takes P straight from TMEM (tcgen05.mma with the A operand in TMEM), so P never
-//     touches shared memory;
-//   * warp 8 lane 0 (TMA): both Q tiles once, then K_0, V_0, K_1, V_1, ... through a
-//     5-slot ring of 128-key blocks (128B swizzle, zero fill past seq_kv);
-//   * warp 9 (MMA; the warp waits, an elected lane issues): per key block j the tensor core runs PV_0(j), QK_0(j+1),
-//     PV_1(j), QK_1(j+1): while one tile's softmax works, the other tile's two products
-//     run. MMAs of one thread execute in order, so QK_t(j+1) overwriting S_t/P_t after
-//     PV_t(j) read P_t is ordered, and the commit that announces S_t(j+1) also covers
-//     PV_t(j): a softmax that sees S_t(j+1) may rescale O_t and rewrite P_t at once;
-//   * warps 0-3 / 4-7 (softmax, one warpgroup per tile): thread = query row, the whole
-//     128-key row sits in registers, so max and sum need no shuffles; exp2 in the log2
-//     domain with the scale folded in; the O rescale is lazy (only when the running max
-//     grows by more than 2^8, which keeps every p <= 256) and done in TMEM by the same
-//     warp;
+//   * TMEM: S | P_0 | P_1 | O_0 | O_1 = 128 + 64 + 64 + 128 + 128 = 512 columns. One S buffer
+//     serves both tiles in turn: a softmax warpgroup copies its S into registers and frees
+//     the buffer at once, so the other tile's Q·Kᵀ runs while this tile's softmax works. P_t
+//     (16-bit pairs, 64 columns) has its own columns, and the P·V product takes P straight
+//     from TMEM (tcgen05.mma with the A operand in TMEM), so P never touches shared memory;
+//   * warp 10 lane 0 (TMA): both Q tiles once, then the K/V blocks through a 5-slot ring of
+//     128-key blocks in the order the products release them, K_0, K_1, V_0, K_2, V_1, ...
+//     (128B swizzle, zero fill past seq_kv);
+//   * warps 0 and 1 (MMA issuers; each warp waits, an elected lane issues): warp 0 runs the
+//     Q·Kᵀ products into the S buffer in the order S_0(0), S_1(0), S_0(1), S_1(1), ..., each
+//     once the previous S has been copied out; warp 1 runs the P·V products, each once its
+//     tile's P is stored. A softmax warpgroup stores P_t(j), copies S_t(j+1) out and only
+//     then announces both, so the other tile's next Q·Kᵀ (which that softmax waits for)
+//     goes to the tensor core first and this P·V (needed only at this tile's next P store)
+//     after it. The two softmax warpgroups run side by side, half a block apart;
+//   * warps 2-5 / 6-9 (softmax, one warpgroup per tile; each covers the four TMEM lane
+//     quarters, warp % 4): thread = query row, the whole 128-key row sits in registers, so
+//     max and sum need no shuffles; exp2 in the log2 domain with the scale folded in; the O
+//     rescale is lazy (only when the running max grows by more than 2^8, which keeps every
+//     p <= 256) and done in TMEM by the same warp after the tile's previous P·V has finished
+//     (which also frees P_t);
 //   * persistent: one CTA per SM takes (head, query-tile pair) items from a global counter,
 //     head by head and the heaviest causal pair of a head first, so the items in flight
 //     share a few heads' K/V blocks in L2; the TMA warp publishes the next item through a
@@ -36,7 +41,9 @@
 
 namespace lvb {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 352;
+// Warp roles: the two MMA issuers, the TMA producer; warps 2-9 are the softmax warpgroups.
+constexpr int kQkWarp = 0, kPvWarp = 1, kTmaWarp = 10;
 constexpr int kChunk = 128 * 128;       // bytes of one 128-row x 64-element swizzled chunk
 
 struct AttnParams {
@@ -66,6 +73,21 @@ __device__ __forceinline__ void drain_wait_a(uint64_t* bar, uint32_t parity, uin
   while (!bar_try_wait(a, parity)) {
     if (global_ns() - t0 > timeout_ns) return;
   }
+}
+
+// Ring order of an item's K/V blocks: K_0, K_1, V_0, K_2, V_1, ..., K_{nb-1}, V_{nb-2},
+// V_{nb-1} — the order in which the products release them (K_{j+1} with the second tile's
+// Q·Kᵀ, V_j with its P·V, half a block later), so each load has about two blocks of slack.
+__device__ __forceinline__ int ring_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int ring_v(int j, int nb) { return j + 1 < nb ? 2 * j + 2 : 2 * j + 1; }
+
+// An issuer's wait: a non-blocking test first (a completed phase is the common case and
+// mbarrier.try_wait costs far more even then), the bounded suspending wait otherwise.
+__device__ __forceinline__ bool issuer_wait(uint64_t* bar, uint32_t parity, const WaitGuard& g,
+                                            int where, int detail) {
+  bool ok = bar_test_wait(smem_u32(bar), parity);
+  if (!__all_sync(0xffffffffu, ok)) ok = wait_bar_warp(bar, parity, g, where, detail);
+  return ok;
 }
 
 template <bool BF16>
@@ -121,9 +143,12 @@ __device__ __forceinline__ AttnItem attn_item(int item, const AttnParams& p) {
   return it;
 }
 
-// 10 warps: three share a scheduler on two of the four sub-partitions (16,384 registers
+// 11 warps: three share a scheduler on three of the four sub-partitions (16,384 registers
 // each), which caps a thread at 168 registers; the softmax threads keep a 128-key score row
-// in registers within that.
+// in registers within that. Two issuer warps instead of one: an issuing thread cannot run
+// ahead of the tensor core by more than a few MMAs, and a wait costs a warp a few hundred
+// cycles even when the barrier is already complete, so with one warp the tensor core idled
+// through every wait; with two, one warp's products run while the other waits.
 //
 // Persistent: one CTA per SM takes items from a global counter until they run out. The TMA
 // warp takes the next item as soon as it has issued the current one's loads and publishes it
@@ -151,15 +176,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* q_empty = q_full + 1;          // the item's last QK read Q
   uint64_t* ring_full = q_empty + 1;       // [R]
   uint64_t* ring_empty = ring_full + R;    // [R]
-  uint64_t* s_full = ring_empty + R;       // [2] QK_t done (and every MMA before it)
-  uint64_t* p_full = s_full + 2;           // [2] softmax_t wrote P_t (128 arrivals)
+  uint64_t* s_full = ring_empty + R;       // [2] QK_t done: the S buffer holds tile t's S
+  uint64_t* s_free = s_full + 2;           // the S buffer's owner copied it out (4 warps)
+  uint64_t* p_full = s_free + 1;           // [2] softmax_t wrote P_t (4 warps)
   uint64_t* pv_done = p_full + 2;          // [2] PV_t done
   uint64_t* sched_full = pv_done + 2;      // [kSched] item index published
-  uint64_t* sched_empty = sched_full + kSched;   // [kSched] read by the MMA warp and 8 softmax warps
+  uint64_t* sched_empty = sched_full + kSched;   // [kSched] read by 2 MMA warps, 8 softmax warps
   uint64_t* drain = sched_empty + kSched;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* sched_item = reinterpret_cast<volatile int*>(tmem_slot + 2);   // [kSched]
+  // qk_after[t]: Q·Kᵀ products issued right after a copy-out of tile t's S (the P·V warp
+  // lets those go first).
+  volatile int* qk_after = sched_item + kSched;                                 // [2]
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -173,18 +202,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     for (int t = 0; t < 2; ++t) {
       bar_init(&s_full[t], 1);
-      bar_init(&p_full[t], 128);
+      bar_init(&p_full[t], 4);
       bar_init(&pv_done[t], 1);
     }
+    bar_init(s_free, 4);
     for (int s = 0; s < kSched; ++s) {
       bar_init(&sched_full[s], 1);
-      bar_init(&sched_empty[s], 9);
+      bar_init(&sched_empty[s], 10);
     }
-    bar_init(drain, 1);
+    bar_init(drain, 2);
     *abort_flag = 0;
+    qk_after[0] = 0;
+    qk_after[1] = 0;
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == kQkWarp) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -194,7 +226,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const WaitGuard g{p.status, abort_flag, p.timeout_ns};
 
-  if (warp == 8) {
+  if (warp == kTmaWarp) {
     if (lane == 0) {
       // ---------------- scheduler + TMA producer ----------------
       tma_prefetch_desc(&tmQ);
@@ -230,10 +262,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             break;
           }
           bar_arrive_expect_tx(&ring_full[s], Cfg::kTileBytes);
-          const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+          // Item i of the ring order: K_0; odd i: K_{(i+1)/2}, or V_{nb-1} for the last;
+          // even i > 0: V_{i/2 - 1}.
+          bool is_k;
+          int blk;
+          if (i == 0) {
+            is_k = true;
+            blk = 0;
+          } else if (i & 1) {
+            blk = (i + 1) >> 1;
+            is_k = blk < it.n_blocks;
+            if (!is_k) blk = it.n_blocks - 1;
+          } else {
+            is_k = false;
+            blk = (i >> 1) - 1;
+          }
+          const CUtensorMap* tm = is_k ? &tmK : &tmV;
           for (int c = 0; c < kDChunks; ++c)
-            tma_load_4d(sRing + s * Cfg::kTileBytes + c * kChunk, tm, c * 64, (i >> 1) * 128,
-                        it.hk, it.b, &ring_full[s]);
+            tma_load_4d(sRing + s * Cfg::kTileBytes + c * kChunk, tm, c * 64, blk * 128, it.hk,
+                        it.b, &ring_full[s]);
         }
       }
       if (!ok) {
@@ -243,34 +290,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           drain_wait_a(&ring_full[i % R], (uint32_t)((i / R) & 1), p.timeout_ns);
       }
     }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer: the whole warp waits, one elected lane issues --------
+  } else if (warp == kQkWarp || warp == kPvWarp) {
+    // ---------------- MMA issuers: one warp the Q·Kᵀ products, one the P·V products ----
+    // The two touch disjoint TMEM columns (S at 0; P_t at 128 + 64t and O_t at 256 + 128t)
+    // and disjoint ring slots (K / V blocks), so while one waits for its next operand the
+    // other's products keep the tensor core busy (an issuing thread cannot run ahead of the
+    // tensor core by much). In each warp the whole warp waits and one elected lane issues a
+    // whole product and its commits, with the shared-memory descriptors precomputed and
+    // advanced in their 16-byte address field.
+    const bool qk_role = warp == kQkWarp;
     const uint32_t q_base = smem_u32(sQ);
     const uint32_t r_base = smem_u32(sRing);
-    auto issue_qk = [&](int t, int slot) {
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t o = (kk >> 2) * kChunk + (kk & 3) * 32;
-        const uint64_t ad = sdesc_sw128(q_base + t * Cfg::kTileBytes + o, 16, 1024);
-        const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + o, 16, 1024);
-        if (elect_one()) mma_f16_ss(tmem + 128 * t, ad, bd, kIdescQK, kk > 0 ? 1u : 0u);
-      }
-    };
-    auto issue_pv = [&](int t, int slot, bool acc) {
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {   // 128 keys, 16 per MMA: P columns 8kk..8kk+7
-        // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64 dims
-        // kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
-        const uint64_t bd = sdesc_sw128(r_base + slot * Cfg::kTileBytes + kk * 16 * 128,
-                                        kChunk, 1024);
-        if (elect_one())
-          mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk, bd, kIdescPV,
-                     (acc || kk > 0) ? 1u : 0u);
-      }
-    };
-    int rc = 0;               // ring items consumed before the current item
+    const uint64_t qd0 = sdesc_sw128(q_base, 16, 1024);
+    const uint64_t kd0 = sdesc_sw128(r_base, 16, 1024);
+    const uint64_t vd0 = sdesc_sw128(r_base, kChunk, 1024);
+    constexpr uint32_t kTile16 = Cfg::kTileBytes >> 4;
+    int rc = 0;               // ring items of the items before the current one
     int qi = 0;               // items with work before the current one
     int gt[2] = {0, 0};       // blocks of each tile before the current item
+    int fills = 0;            // Q·Kᵀ products written to the S buffer so far
+    int prev_tile = 0;        // tile of the last S written
+    int after[2] = {0, 0};    // copy of qk_after (written by the Q·Kᵀ warp only)
     bool ok = true;
     for (int k = 0; ok; ++k) {
       const int sslot = k % kSched;
@@ -283,65 +323,105 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (it.n_blocks == 0) continue;
       const int nt[2] = {it.n_tile0, it.n_tile1};
       const int nb = it.n_blocks;
-      if (!wait_bar_warp(q_full, (uint32_t)(qi & 1), g, 12, item) ||
-          !wait_bar_warp(&ring_full[rc % R], (uint32_t)((rc / R) & 1), g, 13, item)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      for (int t = 0; t < 2; ++t) {
-        if (nt[t] == 0) continue;
-        issue_qk(t, rc % R);
-        if (elect_one()) mma_commit(&s_full[t]);
-      }
-      if (elect_one()) {
-        if (nb == 1) mma_commit(q_empty);         // the item's last QK has been issued
-        mma_commit(&ring_empty[rc % R]);          // K_0
-      }
-      for (int j = 0; j < nb && ok; ++j) {
-        const int iv = rc + 2 * j + 1;            // V_j
-        const int ik = rc + 2 * j + 2;            // K_{j+1}
-        const bool next = j + 1 < nb;
-        if (!wait_bar_warp(&ring_full[iv % R], (uint32_t)((iv / R) & 1), g, 14, j)) {
-          ok = false;
-          break;
+      // Ring item i of this item (ring_k / ring_v); each warp waits for its items in
+      // increasing order, once each (a slot is refilled only after its release).
+      int ring_seen = -1;     // this warp's ring items of the item already waited for
+      auto ring_wait = [&](int i, int where) -> bool {
+        if (i <= ring_seen) return true;
+        const int x = rc + i;
+        if (!issuer_wait(&ring_full[x % R], (uint32_t)((x / R) & 1), g, where, i)) return false;
+        ring_seen = i;
+        return true;
+      };
+      auto release = [&](int i) {
+        if (elect_one()) mma_commit(&ring_empty[(rc + i) % R]);
+        __syncwarp();
+      };
+      if (qk_role) {
+        if (!wait_bar_warp(q_full, (uint32_t)(qi & 1), g, 12, item)) break;
+        const int n_qk = nt[0] + nt[1];
+        int qk_done = 0;
+        // Q·Kᵀ of tile t for key block j into the S buffer, once the previous S is copied
+        // out; the commit on q_empty after the item's last one releases Q.
+        auto fill = [&](int t, int j) -> bool {
+          if (!ring_wait(ring_k(j), 13)) return false;
+          if (fills > 0 && !issuer_wait(s_free, (uint32_t)((fills - 1) & 1), g, 17, j))
+            return false;
+          tc_fence_after();
+          const bool last = ++qk_done == n_qk;
+          if (elect_one()) {
+            const uint64_t ad = qd0 + (uint64_t)(t * kTile16);
+            const uint64_t bd = kd0 + (uint64_t)(((rc + ring_k(j)) % R) * kTile16);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t o = ((kk >> 2) * kChunk + (kk & 3) * 32) >> 4;
+              mma_f16_ss(tmem, ad + o, bd + o, kIdescQK, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&s_full[t]);
+            if (last) mma_commit(q_empty);
+          }
+          __syncwarp();
+          if (fills > 0) {
+            ++after[prev_tile];
+            if (lane == 0) qk_after[prev_tile] = after[prev_tile];
+          }
+          prev_tile = t;
+          ++fills;
+          return true;
+        };
+        // Fill order S_0(0), S_1(0), S_0(1), S_1(1), ...: each softmax warpgroup copies its
+        // next S out when it has finished a block (the first at the item's start), so each
+        // Q·Kᵀ runs while the other tile's softmax works.
+        if (nt[0] > 0) ok = fill(0, 0);
+        if (ok && nt[1] > 0) ok = fill(1, 0);
+        if (ok && nt[0] > 1) ok = fill(0, 1);
+        if (!ok) break;
+        release(0);                                              // K_0
+        for (int j = 0; j < nb && ok; ++j) {
+          if (j + 1 < nt[1]) ok = fill(1, j + 1);
+          if (ok && j + 2 < nt[0]) ok = fill(0, j + 2);
+          if (!ok) break;
+          if (j + 1 < nb) release(ring_k(j + 1));                // K_{j+1}: last use
         }
-        bool k_ready = false;
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (j < nt[t]) {
-            if (!wait_bar_warp(&p_full[t], (uint32_t)((gt[t] + j) & 1), g, 15, j)) {
+      } else {
+        for (int j = 0; j < nb && ok; ++j) {
+          if (!ring_wait(ring_v(j, nb), 14)) { ok = false; break; }
+          for (int t = 0; t < 2; ++t) {
+            if (j >= nt[t]) continue;
+            if (!issuer_wait(&p_full[t], (uint32_t)((gt[t] + j) & 1), g, 15, j)) {
               ok = false;
               break;
+            }
+            // P_t(j) was announced together with the copy-out of S_t(j+1), which lets the
+            // other tile's next Q·Kᵀ into the S buffer; that product is on the critical path
+            // (the other softmax waits for it), this P·V is not (it is needed at this tile's
+            // next P store), so let the Q·Kᵀ reach the tensor core first. A priority hint
+            // only: after ~2 us the P·V goes anyway.
+            if (j + 1 < nt[t] && !(t == 1 && j + 2 == nt[1] && nt[1] >= nt[0])) {
+              const int target = gt[t] + j + 2;
+              if (qk_after[t] < target) {
+                const uint64_t t0 = global_ns();
+                while (qk_after[t] < target && global_ns() - t0 < 2000) {
+                }
+              }
+              __syncwarp();
             }
             tc_fence_after();
-            issue_pv(t, iv % R, j > 0);
-            if (elect_one()) mma_commit(&pv_done[t]);
-          }
-          if (j + 1 < nt[t]) {
-            if (!k_ready) {
-              if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
-                ok = false;
-                break;
-              }
-              k_ready = true;
+            if (elect_one()) {
+              // V block: rows are keys (128 B = 64 head-dim elements each), chunks of 64
+              // dims kChunk bytes apart: MN-major, SBO = 8 key rows, LBO = next 64-dim chunk.
+              const uint64_t bd = vd0 + (uint64_t)(((rc + ring_v(j, nb)) % R) * kTile16);
+              const uint32_t tp = tmem + 128 + 64 * t;
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk)   // 128 keys, 16 per MMA: P columns 8kk..8kk+7
+                mma_f16_ts(tmem + 256 + 128 * t, tp + 8 * kk, bd + (uint64_t)(kk * 128),
+                           kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+              mma_commit(&pv_done[t]);
             }
-            issue_qk(t, ik % R);
-            if (elect_one()) mma_commit(&s_full[t]);
+            __syncwarp();
           }
-        }
-        if (!ok) break;
-        if (elect_one()) {
-          if (j == nb - 2) mma_commit(q_empty);   // the item's last QK has been issued
-          mma_commit(&ring_empty[iv % R]);        // V_j done (both tiles)
-        }
-        if (next) {
-          if (!k_ready) {  // no tile used K_{j+1}: still consume it in order
-            if (!wait_bar_warp(&ring_full[ik % R], (uint32_t)((ik / R) & 1), g, 16, j)) {
-              ok = false;
-              break;
-            }
-          }
-          if (elect_one()) mma_commit(&ring_empty[ik % R]);   // K_{j+1} done
+          if (!ok) break;
+          release(ring_v(j, nb));                                // V_j
         }
       }
       rc += 2 * nb;
@@ -353,11 +433,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     drain_wait_a(drain, 0, p.timeout_ns);
   } else {
     // ---------------- softmax, one warpgroup per query tile ----------------
-    const int t = warp >> 2;
+    const int t = (warp - 2) >> 2;
     const int wl = warp & 3;
     const int r = wl * 32 + lane;               // row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(wl * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * t;        // S_t, then P_t in its first 64 cols
+    const uint32_t tS = tmem + lane_off;                  // the S buffer (shared)
+    const uint32_t tP = tmem + lane_off + 128 + 64 * t;   // P_t
     const uint32_t tO = tmem + lane_off + 256 + 128 * t;
     const float NEG_INF = -INFINITY;
     const int off = p.Skv - p.Sq;
@@ -378,9 +459,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int tile_first_row = it.q0 + 128 * t;
       const int nt = it.n_blocks == 0 ? 0 : (t ? it.n_tile1 : it.n_tile0);
 
+      // S_t(j) is copied into registers right after P_t(j-1) is stored, and only then is
+      // P_t(j-1) announced: the MMA warp, which runs the other tile's next Q·Kᵀ (into the S
+      // buffer) before this tile's P·V, learns both at once.
       for (int j = 0; j < nt; ++j) {
-        // S_t(j) ready; PV_t(j-1) (so O_t, and the P_t columns) is complete too.
-        if (!wait_bar(&s_full[t], (uint32_t)((gt + j) & 1), g, 21, j)) { ok = false; break; }
+        if (!wait_bar_warp(&s_full[t], (uint32_t)((gt + j) & 1), g, 21, j)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         uint32_t s[128];
         tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
@@ -388,101 +474,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
         tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
         tmem_wait_ld();
-
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (j > 0) bar_arrive(&p_full[t]);
+          bar_arrive(s_free);
+        }
         const int kbase = j * 128;
         const bool need_mask =
             (kbase + 127 >= p.Skv) || (p.causal && kbase + 127 > tile_first_row + off);
-        const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
-        auto mask = [&]() {
-          if (need_mask) {
+        if (need_mask) {
+          const int lim = p.causal ? min(q + off, p.Skv - 1) : p.Skv - 1;
 #pragma unroll
-            for (int c = 0; c < 128; ++c)
-              if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
-          }
-        };
+          for (int c = 0; c < 128; ++c)
+            if (kbase + c > lim) s[c] = __float_as_uint(NEG_INF);
+        }
         const float sl = p.scale_log2;
-        // p = 2^(s·scale·log2e - m) for the row, packed pairwise in place over s[0..63];
-        // returns the row sum (4 independent chains).
-        auto exps = [&](float m_use) {
-          float sump[4] = {0.f, 0.f, 0.f, 0.f};
+        // Row max: 4 independent chains of 3-input maxima.
+        float mxp[4];
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
-            sump[c & 3] += p0 + p1;
-            s[c] = pack2<BF16>(p0, p1);
-          }
-          return (sump[0] + sump[1]) + (sump[2] + sump[3]);
-        };
-        mask();
-
-        // Lazy rescaling needs the block's row max only when it exceeds the running max by
-        // more than 2^8. So from the second block on, exponentiate against the running max
-        // first: a row sum <= 256 proves every p <= 2^8 and the block is done. Otherwise
-        // (or on the first block, or for a row with no key yet) the warp reloads S from
-        // TMEM, takes the true max and recomputes; a row that passed the first test
-        // recomputes the same values.
+        for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
+#pragma unroll
+        for (int c = 4; c < 124; c += 8)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            mxp[i] = fmax3(mxp[i], __uint_as_float(s[c + i]), __uint_as_float(s[c + 4 + i]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[124 + i]));
+        const float m_new = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])) * sl;
         float alpha = 1.f;
         bool resc = false;
-        float sum = 0.f;
-        bool done = false;
+        if (j == 0) {
+          m_ref = m_new;
+        } else if (m_new > m_ref + 8.f) {
+          alpha = fast_exp2(m_ref - m_new);
+          m_ref = m_new;
+          resc = true;
+        }
+        // p = 2^(s·scale·log2e - m) for the row, packed pairwise in place over s[0..63]
+        // (4 independent sum chains).
+        const float m_use = m_ref == NEG_INF ? 0.f : m_ref;
+        float sump[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[2 * c]), sl, -m_use));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[2 * c + 1]), sl, -m_use));
+          sump[c & 3] += p0 + p1;
+          s[c] = pack2<BF16>(p0, p1);
+        }
+        const float sum = (sump[0] + sump[1]) + (sump[2] + sump[3]);
+        // PV_t(j-1) has finished: P_t may be rewritten and O_t rescaled.
         if (j > 0) {
-          sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
-          done = (m_ref != NEG_INF) && (sum <= 256.f);
-        }
-        if (!__all_sync(0xffffffffu, done)) {
-          if (j > 0) {
-            tmem_ld32(tS + 0, *reinterpret_cast<uint32_t (*)[32]>(&s[0]));
-            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t (*)[32]>(&s[32]));
-            tmem_ld32(tS + 64, *reinterpret_cast<uint32_t (*)[32]>(&s[64]));
-            tmem_ld32(tS + 96, *reinterpret_cast<uint32_t (*)[32]>(&s[96]));
-            tmem_wait_ld();
-            mask();
+          if (!wait_bar_warp(&pv_done[t], (uint32_t)((gt + j - 1) & 1), g, 22, j)) {
+            ok = false;
+            break;
           }
-          // Row max as 4 independent chains (one chain would serialise 128 dependent maxes).
-          float mxp[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) mxp[i] = __uint_as_float(s[i]);
-#pragma unroll
-          for (int c = 4; c < 128; c += 4)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) mxp[i] = fmaxf(mxp[i], __uint_as_float(s[c + i]));
-          const float mx = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-          const float m_new = mx * sl;
-          if (j == 0) {
-            m_ref = m_new;
-          } else if (m_new > m_ref + 8.f) {
-            alpha = fast_exp2(m_ref - m_new);
-            m_ref = m_new;
-            resc = true;
-          }
-          sum = exps(m_ref == NEG_INF ? 0.f : m_ref);
-        }
-        // P_t (64 packed columns) over the first half of S_t: the MMA's A operand.
-        tmem_st32(tS + 0, &s[0]);
-        tmem_st32(tS + 32, &s[32]);
-        if (j > 0 && __any_sync(0xffffffffu, resc)) {
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(tO + 16 * c, o);
-            tmem_wait_ld();
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t o[16];
+              tmem_ld16(tO + 16 * c, o);
+              tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st16(tO + 16 * c, o);
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st16(tO + 16 * c, o);
+            }
           }
         }
+        tmem_st32(tP + 0, &s[0]);
+        tmem_st32(tP + 32, &s[32]);
         tmem_wait_st();
         l = l * alpha + sum;
         tc_fence_before();
-        bar_arrive(&p_full[t]);
       }
       if (!ok) break;
+      if (nt > 0) {
+        __syncwarp();
+        if (lane == 0) bar_arrive(&p_full[t]);    // the last block's P
+      }
 
       // ---------------- epilogue: O / l -> global, lse ----------------
       // O_t is rewritten by the next item's first P·V only after this warpgroup has
       // produced that item's first P, i.e. after these loads have completed.
-      if (nt > 0 && !wait_bar(&pv_done[t], (uint32_t)((gt + nt - 1) & 1), g, 23, 0)) break;
+      if (nt > 0 && !wait_bar_warp(&pv_done[t], (uint32_t)((gt + nt - 1) & 1), g, 23, 0)) break;
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = q < p.Sq;
@@ -528,7 +603,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kQkWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -526,6 +526,13 @@ __device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* v) {
                : "memory");
 }
 
+// Maximum of three (sm_100's three-input max.f32).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
