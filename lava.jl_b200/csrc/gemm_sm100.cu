@@ -588,6 +588,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+  // Launched with programmatic stream serialization: the setup above may have run while the
+  // previous kernel of the stream was finishing; global memory is touched only after it has
+  // completed. The next GEMM may start its own setup now (this grid is all resident already).
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
@@ -1205,8 +1210,20 @@ int launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td
     if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cudaFuncSetAttribute");
     attr_set[dv].store(true, std::memory_order_release);
   }
-  kern<<<ctas, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, td, p);
-  e = cudaGetLastError();
+  // Programmatic stream serialization: a small GEMM's launch latency and setup (barriers,
+  // TMEM allocation, descriptor prefetch) overlap the previous kernel of the stream; the
+  // kernel waits for that kernel before its first global memory access.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "kernel launch");
   return LVB_OK;
 }

@@ -526,6 +526,16 @@ __device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* v) {
                : "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next kernel of the stream, when
+// it was launched with programmatic stream serialization, start on free SMs (its setup runs
+// while this kernel works); wait blocks until the previous kernel of the stream has completed
+// and its memory is visible — a kernel that allows an early start calls it before touching
+// global memory. Both are no-ops for kernels launched without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Maximum of three (sm_100's three-input max.f32).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float y;
