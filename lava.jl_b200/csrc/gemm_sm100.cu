@@ -798,6 +798,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+  // Programmatic stream serialization, as in the one-CTA kernel: global memory only after
+  // the previous kernel of the stream has completed; the next may be scheduled now (it gets
+  // SMs as this grid's CTAs exit).
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -1009,6 +1014,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitGuard g{p.status, abort_flag, p.timeout_ns};
+  // Programmatic stream serialization, as in the one-CTA kernel: global memory only after
+  // the previous kernel of the stream has completed; the next may be scheduled now (it gets
+  // SMs as this grid's CTAs exit).
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -1244,7 +1254,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     attr_set[dva].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -1269,6 +1279,9 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     clusters = std::min(clusters, resident[dva]);
   }
   cfg.gridDim = dim3(2 * std::max(1, clusters));
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cluster kernel launch");
   return LVB_OK;
@@ -1288,7 +1301,7 @@ int launch_tall(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     attr_set[dva].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
@@ -1313,6 +1326,9 @@ int launch_tall(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     clusters = std::min(clusters, resident[dva]);
   }
   cfg.gridDim = dim3(2 * std::max(1, clusters));
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, p);
   if (e != cudaSuccess) return fail_cuda(e, "lvb_gemm", "cluster kernel launch");
   return LVB_OK;
