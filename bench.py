@@ -523,8 +523,9 @@ def attention_shard(torch, lvb, name, world, rank):
     plan = lvb.attention_plan(n, g, 1, S, S, D, lvb.F16 if w["ab"] == "Float16" else lvb.BF16,
                               True, sm_count=torch.cuda.get_device_properties(0).multi_processor_count)
 
-    def step():
-        lvb.attention(O, Q, K, V, causal=True)
+    # One foreign call per step (the descriptor is built once): at N = 8 a rank's share is
+    # ~70 us of kernel time, and eight ranks share the host's cores.
+    step = lvb.prepare_attention(O, Q, K, V, causal=True)
     return w, step, flop_local, flop_total, plan.launches, (Q, K, V, O), n
 
 
@@ -569,9 +570,12 @@ def measure_extras(args, torch, lvb, world, rank, local, stream, sync, max_over_
     sms = torch.cuda.get_device_properties(local).multi_processor_count
     plan = lvb.gemm_plan(max(rn, 1), N, K, lvb.I8, lvb.I32, c_rowmajor=True, sm_count=sms)
 
+    # One foreign call per step (prepared once): a 1024-row shard is ~47 us of kernel time.
+    gcall = lvb.prepare_gemm(Cm, A, Bm.t()) if rn else None
+
     def gstep():
-        if rn:
-            lvb.gemm(Cm, A, Bm.t())
+        if gcall is not None:
+            gcall()
     ms_l, ms, clocks = timed_region(torch, gstep, args.steps, args.warmup, stream, local, sync,
                                     max_over_ranks)
     st = lvb.device_status()

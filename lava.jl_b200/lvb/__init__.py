@@ -546,6 +546,36 @@ def attention(O, Q, K, V, causal=True, scale=None, lse=None, stream=None):
     return O
 
 
+class AttentionCall:
+    """An attention forward described once, launched many times: ``a = prepare_attention(O,
+    Q, K, V, ...)`` then ``a()`` (or ``a(stream)``) — one foreign call per launch. The tensors
+    must stay alive and keep their storage while the object is used."""
+
+    def __init__(self, O, Q, K, V, causal=True, scale=None, lse=None):
+        self.d = attention_desc(O, Q, K, V, causal, scale)
+        self.keep = (O, Q, K, V, lse)
+        self._args = (C.byref(self.d), Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                      lse.data_ptr() if lse is not None else None)
+        self._default_stream = None
+
+    def __call__(self, stream=None):
+        if stream is None:
+            if self._default_stream is None:
+                self._default_stream = _stream_ptr(None)
+            s = self._default_stream
+        else:
+            s = _stream_ptr(stream)
+        st = lib.lvb_attention_fwd(*self._args, s)
+        if st:
+            check(st)
+
+
+def prepare_attention(O, Q, K, V, causal=True, scale=None, lse=None) -> AttentionCall:
+    """See ``AttentionCall``; arguments as ``attention``'s. The default stream is torch's
+    current stream at the first call."""
+    return AttentionCall(O, Q, K, V, causal, scale, lse)
+
+
 ATTN_FLASH, ATTN_DECODE, ATTN_EMPTY = 0, 1, 2
 
 

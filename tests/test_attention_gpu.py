@@ -183,3 +183,21 @@ def test_config4_fp16_full(lvb, torch_cuda):
 @pytest.mark.slow
 def test_config5_bf16_gqa_full(lvb, torch_cuda):
     _full_config(lvb, torch_cuda, "C5", _units(8, 64, 8, 16))
+
+
+def test_prepared_call_matches_one_shot_call(lvb, torch_cuda):
+    """lvb.prepare_attention (descriptor built once) gives exactly lvb.attention's result."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(5)
+    Q = torch.randn(2, 8, 1024, 128, device="cuda", dtype=torch.float16, generator=g)
+    K = torch.randn(2, 4, 1024, 128, device="cuda", dtype=torch.float16, generator=g)
+    V = torch.randn(2, 4, 1024, 128, device="cuda", dtype=torch.float16, generator=g)
+    ref = torch.empty_like(Q)
+    lvb.attention(ref, Q, K, V, causal=True)
+    O = torch.zeros_like(Q)
+    a = lvb.prepare_attention(O, Q, K, V, causal=True)
+    for _ in range(3):
+        a()
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    assert torch.equal(O, ref)

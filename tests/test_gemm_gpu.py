@@ -383,3 +383,26 @@ def test_tall_pair_tile(lvb, torch_cuda, M, N, K, ab, out, c_rowmajor):
     A, Bt = gemm_inputs(M, N, K, ab, seed=M + K)
     C = run(lvb, torch_cuda, A, Bt, ab, out, c_rowmajor=c_rowmajor)
     check(C, A, Bt.T, out)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (1024, 8192, 1024)])
+def test_prepared_call_matches_one_shot_call(lvb, torch_cuda, M, N, K):
+    """lvb.prepare_gemm (descriptor built once, one foreign call per launch; the one-CTA kernel
+    at 512³ and the pair kernel at the larger shape, both launched with programmatic stream
+    serialization) gives exactly lvb.gemm's result, call after call, with a dependent kernel
+    (torch's add_) between launches on the same stream."""
+    torch = torch_cuda
+    A, Bt = gemm_inputs(M, N, K, "Float16", 11)
+    dA = torch.from_numpy(A).half().cuda()
+    dB = torch.from_numpy(np.ascontiguousarray(Bt)).half().cuda().t()   # K x N, column-major
+    ref = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    lvb.gemm(ref, dA, dB)
+    C = torch.full((M, N), 3.0, dtype=torch.float32, device="cuda")
+    g = lvb.prepare_gemm(C, dA, dB)
+    for _ in range(5):
+        g()
+        C.add_(1.0)          # reads the GEMM's output: ordered after it on the stream
+        g()                  # overwrites C: ordered after the add_
+    torch.cuda.synchronize()
+    assert lvb.device_status() == (0, 0, 0)
+    assert torch.equal(C, ref)
