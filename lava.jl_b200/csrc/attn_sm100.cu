@@ -459,9 +459,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int tile_first_row = it.q0 + 128 * t;
       const int nt = it.n_blocks == 0 ? 0 : (t ? it.n_tile1 : it.n_tile0);
 
-      // S_t(j) is copied into registers right after P_t(j-1) is stored, and only then is
-      // P_t(j-1) announced: the MMA warp, which runs the other tile's next Q·Kᵀ (into the S
-      // buffer) before this tile's P·V, learns both at once.
+      // S_t(j) is copied into registers right after P_t(j-1) is stored, and only then are
+      // both announced: the Q·Kᵀ warp then writes the next S (usually the other tile's) into
+      // the freed buffer, and the P·V warp lets that product go before this tile's P·V.
       for (int j = 0; j < nt; ++j) {
         if (!wait_bar_warp(&s_full[t], (uint32_t)((gt + j) & 1), g, 21, j)) {
           ok = false;
