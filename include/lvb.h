@@ -21,6 +21,12 @@
  *    side failure (a bounded wait that expired) is recorded in a per-device status word
  *    that lvb_device_status() reads, like Lava's exception flag word that the host checks
  *    at the next synchronisation (src/compiler/entry_wrapper.jl:9-11,199-216).
+ *  - The GEMM kernels are launched with programmatic stream serialization: they may be
+ *    scheduled while the stream's previous kernel ends but touch global memory only after
+ *    it has completed (griddepcontrol.wait), and they let the next kernel be scheduled
+ *    early. A caller's kernel launched after a GEMM with that same attribute must wait
+ *    (griddepcontrol.wait) before reading the GEMM's output; other kernels see plain stream
+ *    order.
  *  - The library never frees caller memory and holds no pointer past a call.
  */
 #ifndef LVB_H
